@@ -1,0 +1,366 @@
+#!/usr/bin/env python3
+"""Benchmark of the ternocl_b200 hot path (one JSON line on rank 0).
+
+Workload (the benchmark's headline configuration): M=1 int2 upconvert GEMV, fp16,
+on the four Llama-3-8B decode shapes (K, N) = (4096, 6144), (4096, 4096),
+(4096, 28672), (14336, 4096); ternary weights uniform over {-1,0,+1}, group-128
+scales uniform [0.01, 0.05], activations N(0, 1); distinct weight sets rotated so
+that more than 2 GiB of weights stream (every call reads its weights from HBM, none
+from the 126 MB L2).  One step = one GEMV per shape, each on the next weight set.
+
+  value      weight-stream GB/s (B + S bytes / time, all ranks), inputs resident in HBM
+  e2e        same metric through the C ABI with host buffers: activations copied
+             host->device and outputs device->host inside the timed region
+  roofline   the GEMV kernel's weight bytes per launch / its mean launch time vs the
+             measured HBM copy bandwidth (MEASURED_PEAKS.json)
+  cpu_baseline  the reference's own host gold (compute_gold, compiled from the
+             reference sources into oracle/_ref) on the host cores, bounded sample
+
+With N GPUs (torchrun) the weight columns of every layer are split across the ranks
+and the outputs are all-gathered over NCCL inside the timed region (strong scaling).
+`--impl reference` times the reference's CPU implementation of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [(4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096)]  # (K, N), Llama-3-8B
+M = 1
+WEIGHTS_GIB = 2.0
+METRIC = "M=1 int2 GEMV weight-stream HBM GB/s"
+WORKLOAD = "llama3-8b decode GEMV sweep, int2_fp16_upcvt, M=1, fp16 (configs[1])"
+
+
+def weight_bytes(K, N):
+    return K * N // 4 + (K // 128) * N * 2
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM traffic of the GEMV from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "int2_gemv_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons, active = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for nm, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU reference arm
+def cpu_reference_sample(budget_s=8.0):
+    """The reference's compute_gold (oracle/_ref) on this host's cores: returns
+    (weight GB/s, threads, sample description)."""
+    from oracle import api as orc
+    from ternocl_b200 import synth
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    rng = np.random.default_rng(0)
+    cases = []
+    for K, N in SHAPES:
+        A = synth.activations(rng, M, K, 0)
+        B = synth.pack_int2(synth.ternary(rng, K, N))
+        S = synth.scales(rng, K, N, 0)
+        cases.append((A, B, S, K, N))
+    use_ref = orc.ref_available()
+    gold = orc.Ref.int2_gold if use_ref else (lambda A, B, S, M_, K, N, bf: orc.int2_gold(A, B, S, M_, K, N, bf))
+    t0 = time.perf_counter()
+    steps, nbytes = 0, 0
+    while True:
+        for A, B, S, K, N in cases:
+            gold(A, B, S, M, K, N, 0)
+            nbytes += weight_bytes(K, N)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return (nbytes / el / 1e9, threads, "reference" if use_ref else "port",
+            "%d passes over the 4 shapes (%.1f s, seed 0, M=1 fp16)" % (steps, el))
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    desc = None
+    for _ in range(args.warmup):
+        cpu_reference_sample(budget_s=0.5)
+    for _ in range(args.steps):
+        v, cores, kind, desc = cpu_reference_sample(budget_s=max(1.0, 20.0 / max(args.steps, 1)))
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic", "config": {"workload": WORKLOAD, "M": M, "shapes_KxN": SHAPES},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": desc},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--sets", type=int, default=0,
+                    help="weight sets to rotate (default: enough for %.0f GiB)" % WEIGHTS_GIB)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import ternocl_b200 as tl
+    from ternocl_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    tl.set_option(tl.OPT_PDL, 0 if args.no_pdl else 1)
+
+    # per-rank column slices (multiples of 16)
+    def cols(N):
+        per = (N // world) // 16 * 16
+        n0 = rank * per
+        return n0, (per if rank < world - 1 else N - n0)
+
+    set_bytes = sum(weight_bytes(K, cols(N)[1]) for K, N in SHAPES)
+    full_set_bytes = sum(weight_bytes(K, N) for K, N in SHAPES)
+    nsets = args.sets or max(1, int(np.ceil(WEIGHTS_GIB * (1 << 30) / full_set_bytes)))
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    layers = []  # per shape: dict
+    for K, N in SHAPES:
+        n0, nl = cols(N)
+        rng = np.random.default_rng(K * 7 + N)
+        A = torch.randn(M, K, generator=g, device=dev).half()
+        # one packed set generated on the host (uniform ternary), further sets are
+        # device-side permutations of its words -> distinct data, same distribution
+        B0 = torch.from_numpy(synth.pack_int2(synth.ternary(rng, K, nl)).view(np.int32)).to(dev)
+        Bs, Ss = [], []
+        for s in range(nsets):
+            perm = torch.randperm(B0.numel(), generator=g, device=dev)
+            Bs.append(B0.view(-1)[perm].view_as(B0).contiguous())
+            Ss.append((torch.rand(K // 128, nl, generator=g, device=dev) * 0.04 + 0.01).half())
+        C = torch.empty(M, nl, dtype=torch.float16, device=dev)
+        Cfull = torch.empty(world, M, nl, dtype=torch.float16, device=dev) if world > 1 else None
+        ws = tl.Workspace(dev, tl.gemv_workspace_size(M, nl, K))
+        layers.append(dict(K=K, N=N, nl=nl, A=A, B=Bs, S=Ss, C=C, Cfull=Cfull, ws=ws))
+    del B0
+    torch.cuda.synchronize()
+
+    L = tl.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def gemv(ly, s):
+        st = L.ternocl_int2_upcvt(ly["A"].data_ptr(), ly["B"][s].data_ptr(), ly["S"][s].data_ptr(),
+                                  ly["C"].data_ptr(), None, None, M, ly["nl"], ly["K"], 0, 0, 0,
+                                  tl.ALGO_GEMV, ly["ws"].ptr(), ly["ws"].nbytes(), sp)
+        if st != 0:
+            raise tl.TernoclError("ternocl_int2_upcvt", st)
+
+    def step(i):
+        s = i % nsets
+        for ly in layers:
+            gemv(ly, s)
+            if world > 1:
+                dist.all_gather_into_tensor(ly["Cfull"], ly["C"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    # one untimed pass over every set (the reference's warm-up rule) + W warm-up steps
+    for i in range(max(nsets, args.warmup)):
+        step(i)
+    barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = full_set_bytes / (ms_per_step * 1e-3) / 1e9  # all ranks' weights per step
+
+    # kernel-only timing (no collectives) for the roofline: GEMV launches back to back
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev2.record(stream)
+    for i in range(args.steps):
+        s = i % nsets
+        for ly in layers:
+            gemv(ly, s)
+    ev3.record(stream)
+    barrier()
+    kern_ms = ev2.elapsed_time(ev3)
+    launches = args.steps * len(layers)
+    achieved = set_bytes * args.steps / (kern_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+
+    # end to end through the C ABI with host buffers (pinned), rank-local
+    hA = [torch.randn(M, ly["K"]).half().pin_memory() for ly in layers]
+    hC = [torch.empty(M, ly["nl"], dtype=torch.float16).pin_memory() for ly in layers]
+    h2d = sum(x.numel() * 2 for x in hA)
+    d2h = sum(x.numel() * 2 for x in hC)
+
+    def e2e_step(i):
+        s = i % nsets
+        for j, ly in enumerate(layers):
+            ly["A"].copy_(hA[j], non_blocking=True)
+            gemv(ly, s)
+            if world > 1:
+                dist.all_gather_into_tensor(ly["Cfull"], ly["C"])
+            hC[j].copy_(ly["C"], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_step(i)
+    barrier()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = full_set_bytes / e2e_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, kind, desc = cpu_reference_sample()
+        cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc}
+
+    if rank == 0:
+        tr = profile_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M": M, "shapes_KxN": SHAPES, "weight_sets": nsets,
+                       "weights_gib": round(nsets * full_set_bytes / 2 ** 30, 3),
+                       "l2": "inputs larger than L2: %d rotating weight sets" % nsets,
+                       "parallelism": "N-sharded columns x%d + NCCL all-gather" % world if world > 1 else "single GPU",
+                       "pdl": not args.no_pdl},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "kernel": "int2_gemv_kernel", "launches": launches,
+                         "bytes_per_step": set_bytes,
+                         "traffic": tr.get("bytes_per_step") if tr else None},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,192 @@
+/* ternocl -- B200 (sm_100a) ternary-weight GEMM/GEMV library, C ABI.
+ *
+ * Drop-in for the TernOCL OpenCL kernels: the same packed weight layouts (int2,
+ * int1 "sel", BITCOS), the same per-128-group scales, the same fused epilogues, the
+ * same N % 16 / K % 128 constraints and ragged-M semantics.  Each entry point takes
+ * the reference kernel's positional arguments in the same order (paths below are
+ * relative to the reference tree); the reference's compile-time -D options (BF16,
+ * POSTOP, OUT_F32, QMODE, HB, TOPK, NUM_EXPERTS) become runtime arguments.
+ *
+ * Conventions
+ *  - All tensor pointers are caller-owned DEVICE pointers; nothing here allocates
+ *    device memory.  16-bit tensors (A, S, SA, SB, C, Other, Bias, RW) are raw
+ *    fp16 or bf16 bits (`dtype`); with out_f32 the output C and Bias are fp32.
+ *  - Other/Bias may be NULL when the epilogue does not read them.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *    stream-ordered and asynchronous; the caller synchronises.
+ *  - Every call returns a ternocl_status; none exits, traps or blocks.
+ *  - Results are deterministic: identical inputs give bit-identical outputs.
+ */
+#ifndef TERNOCL_H
+#define TERNOCL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    TERNOCL_OK = 0,
+    TERNOCL_ERR_SHAPE = 1,      /* N % 16, K % 128, K % HB, ... violated */
+    TERNOCL_ERR_ARG = 2,        /* bad enum / NULL pointer / misaligned pointer */
+    TERNOCL_ERR_CUDA = 3,       /* a CUDA runtime call failed (launch, attribute) */
+    TERNOCL_ERR_TIMEOUT = 4,    /* a bounded device/host wait gave up */
+    TERNOCL_ERR_COMM = 5,       /* multi-GPU communicator error */
+    TERNOCL_ERR_UNSUPPORTED = 6,/* not available on this device / build */
+    TERNOCL_ERR_WORKSPACE = 7   /* workspace too small */
+} ternocl_status;
+
+typedef enum { TERNOCL_FP16 = 0, TERNOCL_BF16 = 1 } ternocl_dtype;
+
+/* Fused epilogue, applied to the fp32 accumulator before the output cast
+ * (common/epilogue.clh:1-37). */
+typedef enum {
+    TERNOCL_POSTOP_NONE = 0,     /* acc */
+    TERNOCL_POSTOP_SILU_MUL = 1, /* acc * sigmoid(acc) * Other[m,n]  (SwiGLU gate) */
+    TERNOCL_POSTOP_ADD = 2,      /* acc + Other[m,n]                (residual)    */
+    TERNOCL_POSTOP_BIAS = 3,     /* acc + Bias[n]                                  */
+    TERNOCL_POSTOP_SIGMOID = 4   /* sigmoid(acc), 0 for acc <= -10                  */
+} ternocl_postop;
+
+/* Kernel choice for the GEMM/GEMV families.  AUTO picks the decode GEMV for small
+ * M and the tensor-core GEMM otherwise (the reference drivers switch at M >= 64,
+ * int2_fp16_upcvt/main.cpp:160). */
+typedef enum { TERNOCL_ALGO_AUTO = 0, TERNOCL_ALGO_GEMV = 1, TERNOCL_ALGO_GEMM = 2 } ternocl_algo;
+
+const char *ternocl_version(void);
+const char *ternocl_status_string(int status);
+/* Last CUDA error string seen by this thread's ternocl calls ("" if none). */
+const char *ternocl_last_error(void);
+
+/* Process-wide options.
+ *  TERNOCL_OPT_PDL (default 0): launch kernels with programmatic dependent launch,
+ *    so a kernel's weight prefetch overlaps the tail of the previous kernel in the
+ *    stream.  Activations and workspaces are only touched after the previous
+ *    kernel has completed; weights (B, S, SR) are read EARLY, so with this option
+ *    on they must not be written by the immediately preceding kernel of the stream.
+ * Returns the previous value, or -1 for an unknown option. */
+typedef enum { TERNOCL_OPT_PDL = 1 } ternocl_option;
+int ternocl_set_option(int option, int value);
+
+/* Workspace (device scratch) a call may use for its cross-CTA split-K partial sums
+ * and arrival counters.  Calls taking `ws` run without it (ws == NULL) at a lower
+ * degree of parallelism.  The workspace must be zero-filled once before its first
+ * use (cudaMemset) and may then be reused by any later call on the same stream;
+ * the counters return to zero by themselves.  Calls that overlap on the GPU need
+ * separate workspaces. */
+size_t ternocl_gemv_workspace_size(int M, int N, int K);
+
+/* ---------------------------------------------------------------------------------
+ * int2 upconvert GEMM/GEMV.  Replaces int2_fp16_upcvt_gemm (int2_fp16_upcvt.cl:196-198)
+ * and int2_fp16_upcvt_gemm_mt (int2_fp16_upcvt.cl:341-343):
+ *   C[m,n] = DT(epi( sum_k A[m,k] * code(B[k,n]) * S[k/128, n] ))
+ *   A : DT [M, K] row-major           B : uint32 [K/16, N], code of row 16kp+j at bits 2j..2j+1,
+ *   S : DT [K/128, N]                     codes {0,1,3} = {0,+1,-1}
+ *   C : DT (or fp32) [M, N]           Other : DT [M, N]     Bias : DT (or fp32) [N]
+ * Requires N % 16 == 0, K % 128 == 0, M >= 1 (any M: ragged tiles are masked).
+ */
+int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,
+                       const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,
+                       int algo, void *ws, size_t ws_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * int1 (binary) upconvert GEMM/GEMV.  Replaces int1_fp16_upcvt_gemm / _gemm_mt
+ * (int1_fp16_upcvt.cl:166-170, 302-306).  B is the device "sel" layout, uint32
+ * [K/32, N]: within K32 row kp and 16-column block n0, word (kp, n0+p) bit j =
+ * sign of (row 32kp + 2p + (j&1), column n0 + j/2), bit 1 = -1
+ * (int1_fp16_upcvt/main.cpp:78-92).  Other arguments as ternocl_int2_upcvt. */
+int ternocl_int1_upcvt(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,
+                       const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,
+                       int algo, void *ws, size_t ws_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * s8 x s2 path (int2_via_int2_x_int8_dpas).
+ *
+ * Activation quantisation pre-kernel, replaces quant_a (int2_int8_dpas.cl:105-106):
+ *   SA[g, m] = DT(127 / max(FLT_EPSILON, max_{k in group g} |A[m,k]|))  (correctly rounded)
+ *   Aq[m, k] = sat_int8(rint(A[m,k] * SA[g,m]))   (round to nearest even; only if Aq != NULL)
+ * SA : DT [K/128, LDSA], LDSA = (M + 31) & ~31 (int2_int8_dpas.cl:58).  Columns m >= M of
+ * SA are not written. */
+int ternocl_int8_ldsa(int M);
+int ternocl_int8_quant_a(const void *A, void *SA, int8_t *Aq, int M, int K, int dtype,
+                         void *stream);
+
+/* s8 x s2 GEMM/GEMV, replaces int2_int8_gemv / int2_int8_gemm_mt
+ * (int2_int8_dpas.cl:213-215, 316-318):
+ *   C[m,n] = DT(epi( sum_g float(sum_{k in g} q[m,k] * code(B[k,n])) * (SB[g,n] * (1/SA[g,m])) ))
+ * with int32 dot products per 128-group.  qmode 0: reads the int8 Aq written by
+ * ternocl_int8_quant_a; qmode 1: quantises A in the kernel from SA (Aq unused).
+ * B as ternocl_int2_upcvt (codes read as 2-bit two's complement). */
+int ternocl_int2_int8(const void *A, const int8_t *Aq, const void *SA, const uint32_t *B,
+                      const void *SB, void *C, const void *Other, const void *Bias, int M, int N,
+                      int K, int dtype, int postop, int out_f32, int qmode, int algo, void *stream);
+
+/* Debug view of the s8 x s2 contraction: Dots[m, g, n] = sum_{k in g} Aq[m,k] * code(B[k,n])
+ * (int32).  Used to check the integer path bit for bit. */
+int ternocl_int2_int8_group_dots(const int8_t *Aq, const uint32_t *B, int32_t *Dots, int M, int N,
+                                 int K, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * BITCOS upconvert GEMM/GEMV, replaces bitcos_fp16_upcvt_gemv / _gemm_mt
+ * (bitcos_fp16_upcvt.cl:179-181, 303-305).  B is one uint32 buffer: bitmap [K/32][N]
+ * (bit c of word (kp,n) = weight(32kp+c, n) != 0) | offsets [N] (first sign word of
+ * column n) | signs (one bit per non-zero, column-major in k, 1 -> -1) | pad
+ * (common/bitcos.hpp:1-8).  SR = slice_ranks [(ls-1), N] for ls K-slices (may be NULL
+ * when ls == 1).  Requires N % 16 == 0, K % 128 == 0, K % (64 * ls) == 0. */
+int ternocl_bitcos_upcvt(const void *A, const uint32_t *B, const void *S, const uint32_t *SR,
+                         int ls, void *C, const void *Other, const void *Bias, int M, int N, int K,
+                         int dtype, int postop, int out_f32, int algo, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Sign flip + blockwise normalised Walsh-Hadamard transform, replaces hadamard_fwht
+ * (hadamard/hadamard_fwht.cl:63-64):  y = H_HB(s .* x) / sqrt(HB) per HB-wide block of
+ * each row of x [rows, K]; signs int8 +-1 [K] (ignored when use_signs == 0).
+ * HB in {256, 512, 1024, 2048, 4096}, K % HB == 0.  y may alias x. */
+int ternocl_hadamard_fwht(const void *x, const int8_t *signs, void *y, int rows, int K, int hb,
+                          int use_signs, int dtype, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * int2 MoE prefill (int2_moe/int2_moe_prefill.cl).  G = T * topk routed rows.
+ *
+ * Route, replaces int2_moe_route (int2_moe_prefill.cl:30-31): from ids[G] (expert of
+ * row g = t*topk + j) build meta[2E+2] = [E+1 row offsets | E+1 row-tile offsets],
+ * perm[G] (sorted row p -> g, ascending g inside an expert) and inv[G] (g -> p).
+ * rows_per_tile must equal ternocl_moe_rows_per_tile() for ternocl_moe_gemm. */
+int ternocl_moe_rows_per_tile(void);
+int ternocl_moe_route(const int32_t *ids, int32_t *meta, int32_t *perm, int32_t *inv, int G,
+                      int num_experts, int rows_per_tile, void *stream);
+/* Gather, replaces int2_moe_gather (int2_moe_prefill.cl:64): Xs[p] = X[perm[p] / topk]. */
+int ternocl_moe_gather(const void *X, const int32_t *perm, void *Xs, int G, int K, int topk,
+                       void *stream);
+/* Grouped GEMM, replaces int2_moe_gemm_mt (int2_moe_prefill.cl:75-77): for the rows p
+ * of every expert e, C[p, n] = epi(A[p] . B_e[:, n]); B_all [E, K/16, N],
+ * S_all [E, K/128, N]; Other_all [G, N] (POSTOP 1/2).  max_rows = G. */
+int ternocl_moe_gemm(const int32_t *meta, const void *A_all, const uint32_t *B_all,
+                     const void *S_all, void *C_all, const void *Other_all, int G, int N, int K,
+                     int num_experts, int dtype, int postop, int out_f32, void *stream);
+/* Combine, replaces int2_moe_combine (int2_moe_prefill.cl:144-145):
+ * O[t, n] = DT(sum_j RW[t*topk+j] * Y[inv[t*topk+j], n]),  Y fp32 [G, N]. */
+int ternocl_moe_combine(const float *Y, const int32_t *inv, const void *RW, void *O, int T, int N,
+                        int topk, int dtype, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Host-side weight packers (no device work).  Same layouts as the reference's
+ * common/bitcos.hpp and int1 driver.
+ *
+ * BITCOS random ternary weights at zero density z, bit-identical to
+ * bitcos_random() (common/bitcos.hpp:31-78) for the same seed and OpenMP thread
+ * count.  Returns the buffer length in words; writes it when cap >= length. */
+size_t ternocl_bitcos_random(int K, int N, double z, uint64_t seed, uint32_t *out, size_t cap);
+/* Pack codes [K, N] (row-major, values -1/0/+1) into a BITCOS buffer. */
+size_t ternocl_bitcos_pack(const int8_t *codes, int K, int N, uint32_t *out, size_t cap);
+/* slice_ranks [(ls-1), N] (common/bitcos.hpp:81-94). */
+int ternocl_bitcos_slice_ranks(const uint32_t *buf, int K, int N, int ls, uint32_t *out);
+/* int1 per-column bit order [K/32, N] -> device sel layout (int1_fp16_upcvt/main.cpp:80-92). */
+int ternocl_int1_to_sel(const uint32_t *B, uint32_t *out, int K, int N);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TERNOCL_H */

@@ -1,0 +1,113 @@
+"""ternocl_b200: B200-native ternary-weight GEMM/GEMV (host-side Python mirror).
+
+Every function here is a thin wrapper over one C-ABI entry point of libternocl.so
+(include/ternocl.h), taking CUDA torch tensors for device memory: PyTorch is only the
+allocator/stream plumbing, the arithmetic is the library's sm_100a kernels.  The
+argument order mirrors the reference kernels' (A, B, S, C, Other, Bias, M, N, K);
+the reference's compile-time options (dtype, POSTOP, OUT_F32, QMODE, HB, TOPK) are
+keyword arguments.  Errors raise TernoclError; there is no CPU fallback.
+"""
+from ._lib import LIB_PATH, TernoclError, call, header_functions, lib  # noqa: F401
+
+FP16, BF16 = 0, 1
+POSTOP_NONE, POSTOP_SILU_MUL, POSTOP_ADD, POSTOP_BIAS, POSTOP_SIGMOID = range(5)
+ALGO_AUTO, ALGO_GEMV, ALGO_GEMM = 0, 1, 2
+OPT_PDL = 1
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def dtype_code(t):
+    torch = _torch()
+    if t.dtype == torch.float16:
+        return FP16
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise TypeError("activations must be float16 or bfloat16, got %s" % t.dtype)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream):
+    torch = _torch()
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise ValueError("tensors must be contiguous CUDA tensors")
+
+
+def set_option(option, value):
+    return lib().ternocl_set_option(option, int(value))
+
+
+class Workspace:
+    """Zero-initialised device scratch for split-K partials and arrival counters.
+
+    Grows on demand (a growth allocates through torch, outside the kernel call)."""
+
+    def __init__(self, device=None, nbytes=0):
+        self.device = device
+        self.buf = None
+        self.reserve(nbytes)
+
+    def reserve(self, nbytes):
+        torch = _torch()
+        if nbytes and (self.buf is None or self.buf.numel() < nbytes):
+            self.buf = torch.zeros(int(nbytes), dtype=torch.uint8, device=self.device or "cuda")
+        return self
+
+    def ptr(self):
+        return None if self.buf is None else self.buf.data_ptr()
+
+    def nbytes(self):
+        return 0 if self.buf is None else self.buf.numel()
+
+
+def gemv_workspace_size(M, N, K):
+    return lib().ternocl_gemv_workspace_size(M, N, K)
+
+
+def _out(M, N, like, out_f32, out):
+    torch = _torch()
+    if out is not None:
+        return out
+    return torch.empty(M, N, dtype=torch.float32 if out_f32 else like.dtype, device=like.device)
+
+
+def _upcvt(entry, A, B, S, postop, out_f32, other, bias, out, algo, workspace, stream):
+    _check_cuda(A, B, S, other, bias, out)
+    M, K = A.shape
+    N = B.shape[1]
+    C = _out(M, N, A, out_f32, out)
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        workspace.reserve(gemv_workspace_size(M, N, K))
+        ws_ptr, ws_bytes = workspace.ptr(), workspace.nbytes()
+    call(entry, _ptr(A), _ptr(B), _ptr(S), _ptr(C), _ptr(other), _ptr(bias), M, N, K,
+         dtype_code(A), int(postop), int(bool(out_f32)), int(algo), ws_ptr, ws_bytes,
+         _stream(stream))
+    return C
+
+
+def int2_upcvt(A, B, S, postop=0, out_f32=False, other=None, bias=None, out=None, algo=0,
+               workspace=None, stream=None):
+    """C = epi(A @ dequant_int2(B, S)); A [M,K] fp16/bf16, B int32 [K/16,N], S [K/128,N]."""
+    return _upcvt("ternocl_int2_upcvt", A, B, S, postop, out_f32, other, bias, out, algo,
+                  workspace, stream)
+
+
+def int1_upcvt(A, B, S, postop=0, out_f32=False, other=None, bias=None, out=None, algo=0,
+               workspace=None, stream=None):
+    """C = epi(A @ dequant_int1(B, S)); B int32 [K/32,N] in the device sel layout."""
+    return _upcvt("ternocl_int1_upcvt", A, B, S, postop, out_f32, other, bias, out, algo,
+                  workspace, stream)

@@ -1,0 +1,190 @@
+// extern "C" entry points of libternocl: argument validation (the reference's
+// host-side checks, e.g. int2_fp16_upcvt/main.cpp:159), workspace planning and
+// dispatch to the kernel families.  No entry point allocates device memory.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+#include "ternocl.h"
+
+namespace ternocl {
+
+Options &options() {
+    static Options o;
+    return o;
+}
+
+static thread_local char g_last_error[256] = "";
+
+static int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return TERNOCL_OK;
+    std::snprintf(g_last_error, sizeof g_last_error, "%s: %s", cudaGetErrorName(e),
+                  cudaGetErrorString(e));
+    return TERNOCL_ERR_CUDA;
+}
+
+static int sm_count() {
+    static int counts[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (counts[dev] == 0) {
+        int c = 0;
+        if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0)
+            c = 148;
+        counts[dev] = c;
+    }
+    return counts[dev];
+}
+
+static bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// ---------------------------------------------------------------------------------
+// GEMV split-K plan: enough CTAs (4 per SM) to keep every SM streaming.
+struct GemvPlan {
+    int SK = 1;
+    size_t cnt_bytes = 0, part_bytes = 0;
+    size_t total() const { return SK > 1 ? cnt_bytes + part_bytes : 0; }
+};
+
+static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+static GemvPlan gemv_plan(int M, int N, int K, int sk_cap) {
+    GemvPlan p;
+    const int strips = (N + 31) / 32, zb = (M + 7) / 8, G = K / kGS;
+    const long long tiles = (long long)strips * zb;
+    const long long target = 4LL * sm_count();
+    int sk = (int)((target + tiles - 1) / tiles);
+    const int max_sk = G / 4 > 1 ? G / 4 : 1;  // >= 4 groups (one per warp) per CTA
+    if (sk > max_sk) sk = max_sk;
+    if (sk > 16) sk = 16;
+    if (sk > sk_cap) sk = sk_cap;
+    if (sk < 1) sk = 1;
+    p.SK = sk;
+    p.cnt_bytes = round_up((size_t)tiles * sizeof(unsigned), 256);
+    p.part_bytes = (size_t)sk * M * N * sizeof(float);
+    return p;
+}
+
+static int check_gemm_common(const void *A, const void *B, const void *S, const void *C,
+                             const void *Other, const void *Bias, int M, int N, int K, int dtype,
+                             int postop, int out_f32) {
+    if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
+    if (postop < 0 || postop > 4 || (out_f32 != 0 && out_f32 != 1)) return TERNOCL_ERR_ARG;
+    if (M < 0 || N <= 0 || K <= 0) return TERNOCL_ERR_SHAPE;
+    if (N % 16 || K % kGS) return TERNOCL_ERR_SHAPE;  // int2_fp16_upcvt/main.cpp:159
+    if (!A || !B || !S || !C) return TERNOCL_ERR_ARG;
+    if ((postop == 1 || postop == 2) && !Other) return TERNOCL_ERR_ARG;
+    if (postop == 3 && !Bias) return TERNOCL_ERR_ARG;
+    if (!aligned(A, 16) || !aligned(B, 16) || !aligned(S, 16) || !aligned(C, out_f32 ? 16 : 8))
+        return TERNOCL_ERR_ARG;
+    if (Other && !aligned(Other, 8)) return TERNOCL_ERR_ARG;
+    if (Bias && !aligned(Bias, out_f32 ? 8 : 4)) return TERNOCL_ERR_ARG;
+    return TERNOCL_OK;
+}
+
+}  // namespace ternocl
+
+using namespace ternocl;
+
+extern "C" {
+
+const char *ternocl_version(void) { return "ternocl-b200 0.1.0 (sm_100a)"; }
+
+const char *ternocl_status_string(int s) {
+    switch (s) {
+    case TERNOCL_OK: return "ok";
+    case TERNOCL_ERR_SHAPE: return "unsupported shape (need N % 16 == 0 and K % 128 == 0)";
+    case TERNOCL_ERR_ARG: return "invalid argument";
+    case TERNOCL_ERR_CUDA: return "CUDA error";
+    case TERNOCL_ERR_TIMEOUT: return "timed out";
+    case TERNOCL_ERR_COMM: return "communication error";
+    case TERNOCL_ERR_UNSUPPORTED: return "unsupported";
+    case TERNOCL_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+    }
+}
+
+const char *ternocl_last_error(void) { return g_last_error; }
+
+int ternocl_set_option(int option, int value) {
+    if (option == TERNOCL_OPT_PDL) {
+        const int old = options().pdl;
+        options().pdl = value ? 1 : 0;
+        return old;
+    }
+    return -1;
+}
+
+size_t ternocl_gemv_workspace_size(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0 || N % 16 || K % kGS) return 0;
+    return gemv_plan(M, N, K, 1 << 30).total();
+}
+
+int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,
+                       const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,
+                       int algo, void *ws, size_t ws_bytes, void *stream) {
+    int st = check_gemm_common(A, B, S, C, Other, Bias, M, N, K, dtype, postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (algo < TERNOCL_ALGO_AUTO || algo > TERNOCL_ALGO_GEMM) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    GemvArgs a;
+    a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
+    a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.stream = (cudaStream_t)stream;
+    // (the tensor-core GEMM path is selected for large M once available)
+    GemvPlan p = gemv_plan(M, N, K, ws ? 1 << 30 : 1);
+    while (p.SK > 1 && (!ws || p.total() > ws_bytes)) p = gemv_plan(M, N, K, p.SK - 1);
+    if (p.SK > 1) {
+        if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
+        a.SK = p.SK;
+        a.ws_cnt = (unsigned *)ws;
+        a.ws_part = (float *)((char *)ws + p.cnt_bytes);
+    }
+    return cuda_status(int2_gemv_launch(a));
+}
+
+// ---- entry points whose kernels are not built yet: report UNSUPPORTED ----------
+int ternocl_int1_upcvt(const void *, const uint32_t *, const void *, void *, const void *,
+                       const void *, int, int, int, int, int, int, int, void *, size_t, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_int8_ldsa(int M) { return (M + 31) & ~31; }
+int ternocl_int8_quant_a(const void *, void *, int8_t *, int, int, int, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_int2_int8(const void *, const int8_t *, const void *, const uint32_t *, const void *,
+                      void *, const void *, const void *, int, int, int, int, int, int, int, int,
+                      void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_int2_int8_group_dots(const int8_t *, const uint32_t *, int32_t *, int, int, int, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_bitcos_upcvt(const void *, const uint32_t *, const void *, const uint32_t *, int, void *,
+                         const void *, const void *, int, int, int, int, int, int, int, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_hadamard_fwht(const void *, const int8_t *, void *, int, int, int, int, int, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_moe_rows_per_tile(void) { return 128; }
+int ternocl_moe_route(const int32_t *, int32_t *, int32_t *, int32_t *, int, int, int, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_moe_gather(const void *, const int32_t *, void *, int, int, int, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_moe_gemm(const int32_t *, const void *, const uint32_t *, const void *, void *,
+                     const void *, int, int, int, int, int, int, int, void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+int ternocl_moe_combine(const float *, const int32_t *, const void *, void *, int, int, int, int,
+                        void *) {
+    return TERNOCL_ERR_UNSUPPORTED;
+}
+
+}  // extern "C"

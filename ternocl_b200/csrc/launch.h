@@ -1,0 +1,83 @@
+// Host-side launch plumbing shared by the kernel files: argument structs, the
+// compile-time epilogue dispatch and the kernel launcher (with optional
+// programmatic dependent launch).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <type_traits>
+
+#include "ternocl.h"
+
+namespace ternocl {
+
+struct F16;
+struct BF16;
+
+// Process-wide options (ternocl_set_option).
+struct Options {
+    int pdl = 0;  // launch with programmatic stream serialization
+};
+Options &options();
+
+// Arguments of one GEMM/GEMV call after validation.
+struct GemvArgs {
+    const void *A = nullptr;
+    const uint32_t *B = nullptr;
+    const void *S = nullptr;
+    void *C = nullptr;
+    const void *Other = nullptr;
+    const void *Bias = nullptr;
+    int M = 0, N = 0, K = 0;
+    int dtype = 0, postop = 0, out_f32 = 0;
+    int SK = 1;                  // cross-CTA K split
+    float *ws_part = nullptr;    // [SK][M][N] fp32 partials
+    unsigned *ws_cnt = nullptr;  // per-tile arrival counters
+    cudaStream_t stream = nullptr;
+};
+
+template <class T>
+struct type_tag {
+    using type = T;
+};
+
+// Calls f(type_tag<DT>, integral_constant<POSTOP>, integral_constant<OUT_F32>) for
+// the runtime (dtype, postop, out_f32) of `a`.
+template <class Args, class F>
+cudaError_t dispatch_epilogue(const Args &a, F &&f) {
+    auto with_dt = [&](auto dt) -> cudaError_t {
+        auto with_po = [&](auto po) -> cudaError_t {
+            if (a.out_f32) return f(dt, po, std::integral_constant<bool, true>{});
+            return f(dt, po, std::integral_constant<bool, false>{});
+        };
+        switch (a.postop) {
+        case 0: return with_po(std::integral_constant<int, 0>{});
+        case 1: return with_po(std::integral_constant<int, 1>{});
+        case 2: return with_po(std::integral_constant<int, 2>{});
+        case 3: return with_po(std::integral_constant<int, 3>{});
+        default: return with_po(std::integral_constant<int, 4>{});
+        }
+    };
+    if (a.dtype == TERNOCL_BF16) return with_dt(type_tag<BF16>{});
+    return with_dt(type_tag<F16>{});
+}
+
+template <class... KArgs, class... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = options().pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Kernel-family entry points (one per .cu file).
+cudaError_t int2_gemv_launch(const GemvArgs &a);
+
+}  // namespace ternocl

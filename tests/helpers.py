@@ -1,0 +1,81 @@
+"""Shared test helpers: seeded inputs, oracle evaluation and the pass rules."""
+import numpy as np
+
+from oracle import api as orc
+from ternocl_b200 import synth
+
+# BASELINE north_star tolerance on DT outputs vs the fp32 host gold:
+# max relative error <= 2e-3 (fp16) / 1e-2 (bf16), relative to max(|gold|, floor)
+# with floor = 1e-2 * rms(gold) (near-zero gold values cancel; their absolute error
+# is bounded by the fp32 accumulation error of the much larger partial sums).
+REL_TOL = {0: 2e-3, 1: 1e-2}
+F32_REL_TOL = 2e-5
+
+
+def rel_err(out, gold):
+    out = np.asarray(out, np.float64)
+    gold = np.asarray(gold, np.float64)
+    floor = 1e-2 * max(np.sqrt(np.mean(gold ** 2)), 1e-30)
+    return np.max(np.abs(out - gold) / np.maximum(np.abs(gold), floor)) if gold.size else 0.0
+
+
+def ulp_diff(a, b):
+    a = np.asarray(a, np.int32)
+    b = np.asarray(b, np.int32)
+    return int(np.max(np.abs(a - b))) if a.size else 0
+
+
+def check_output(out, gold, bf16, out_f32, what=""):
+    """out/gold: raw DT bits (uint16) or fp32. Asserts the tolerance and returns stats."""
+    if out_f32:
+        e = rel_err(out, gold)
+        assert e <= F32_REL_TOL, "%s fp32 rel err %.3g > %.3g" % (what, e, F32_REL_TOL)
+        return e
+    o = synth.from_dt(out, bf16)
+    g = synth.from_dt(gold, bf16)
+    assert np.all(np.isfinite(o)), what + " non-finite output"
+    e = rel_err(o, g)
+    assert e <= REL_TOL[bf16], "%s rel err %.3g > %.3g (max ulp %d)" % (
+        what, e, REL_TOL[bf16], ulp_diff(out, gold))
+    return e
+
+
+def int2_case(seed, M, K, N, bf16, postop=0, out_f32=False):
+    rng = np.random.default_rng(seed)
+    codes = synth.ternary(rng, K, N)
+    B = synth.pack_int2(codes)
+    S = synth.scales(rng, K, N, bf16)
+    A = synth.activations(rng, M, K, bf16)
+    other, bias = synth.epilogue_operands(rng, postop, out_f32, M, N, bf16)
+    return dict(A=A, B=B, S=S, other=other, bias=bias, codes=codes)
+
+
+def int2_gold_out(c, M, K, N, bf16, postop, out_f32):
+    acc = orc.int2_gold(c["A"], c["B"], c["S"], M, K, N, bf16)
+    return orc.epilogue(postop, out_f32, acc, c["other"], c["bias"], M, N, bf16)
+
+
+def dev_dt(x, bf16):
+    """uint16 DT bits (numpy) -> CUDA torch tensor of dtype float16 / bfloat16."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x).view(np.int16))
+    return t.view(torch.bfloat16 if bf16 else torch.float16).cuda()
+
+
+def dev_u32(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x, np.uint32).view(np.int32)).cuda()
+
+
+def dev_any(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def host_dt(t):
+    """CUDA fp16/bf16 tensor -> uint16 raw bits; fp32 tensor -> float32 array."""
+    import torch
+    t = t.detach().cpu()
+    if t.dtype in (torch.float16, torch.bfloat16):
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()

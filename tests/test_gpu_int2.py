@@ -1,0 +1,68 @@
+"""int2 upconvert GEMV/GEMM on the GPU vs the oracle (the reference's host gold,
+int2_fp16_upcvt/main.cpp:79-98 + common/epilogue.hpp:50-67), through the C ABI."""
+import numpy as np
+import pytest
+
+from helpers import check_output, dev_dt, dev_u32, host_dt, int2_case, int2_gold_out
+
+pytestmark = pytest.mark.gpu
+
+# shapes from the reference validation matrix (int2_fp16_upcvt/validate.sh:8-10) and
+# the Llama-3-8B decode sweep, at sizes the oracle finishes in seconds
+GEMV_SHAPES = [(1, 4096, 4096), (1, 4096, 6144), (4, 6144, 5120), (3, 256, 48), (8, 1024, 512),
+               (1, 128, 16), (2, 512, 272), (5, 2048, 1024), (13, 512, 256), (1, 14336, 512)]
+
+
+def run(tl, c, M, K, N, bf16, postop, out_f32, algo, ws=None):
+    A, B, S = dev_dt(c["A"], bf16), dev_u32(c["B"]), dev_dt(c["S"], bf16)
+    other = dev_dt(c["other"], bf16) if c["other"] is not None else None
+    bias = None
+    if c["bias"] is not None:
+        import torch
+        bias = torch.from_numpy(c["bias"]).cuda() if out_f32 else dev_dt(c["bias"], bf16)
+    out = tl.int2_upcvt(A, B, S, postop=postop, out_f32=out_f32, other=other, bias=bias,
+                        algo=algo, workspace=ws)
+    return host_dt(out)
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("M,K,N", GEMV_SHAPES)
+def test_gemv_parity(cuda, tl, M, K, N, bf16):
+    c = int2_case(100 + M + K + N, M, K, N, bf16)
+    gold = int2_gold_out(c, M, K, N, bf16, 0, False)
+    ws = tl.Workspace()
+    for w in (None, ws):
+        out = run(tl, c, M, K, N, bf16, 0, False, tl.ALGO_GEMV, w)
+        check_output(out, gold, bf16, False, "int2 gemv M=%d K=%d N=%d bf16=%d" % (M, K, N, bf16))
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("postop", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("out_f32", [False, True])
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 512), (3, 2048, 1024)])
+def test_gemv_epilogues(cuda, tl, M, K, N, bf16, postop, out_f32):
+    # validate_epilogues.sh:19-39: every POSTOP x {DT, fp32 out} x dtype
+    c = int2_case(7 * postop + M, M, K, N, bf16, postop, out_f32)
+    gold = int2_gold_out(c, M, K, N, bf16, postop, out_f32)
+    out = run(tl, c, M, K, N, bf16, postop, out_f32, tl.ALGO_GEMV, tl.Workspace())
+    check_output(out, gold, bf16, out_f32, "postop=%d out_f32=%d" % (postop, out_f32))
+
+
+def test_gemv_deterministic(cuda, tl):
+    # main.cpp:351-353: every set reproduces set 0 bit for bit
+    M, K, N = 4, 4096, 2048
+    c = int2_case(5, M, K, N, 0)
+    ws = tl.Workspace()
+    outs = [run(tl, c, M, K, N, 0, 0, False, tl.ALGO_GEMV, ws) for _ in range(3)]
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+
+
+def test_gemv_ragged_rows_untouched(cuda, tl):
+    # rows >= M and columns >= N are never written
+    import torch
+    M, K, N = 3, 512, 48
+    c = int2_case(9, M, K, N, 0)
+    A, B, S = dev_dt(c["A"], 0), dev_u32(c["B"]), dev_dt(c["S"], 0)
+    big = torch.full((M + 2, N), 7.0, dtype=torch.float16, device="cuda")
+    tl.int2_upcvt(A, B, S, out=big[:M], algo=tl.ALGO_GEMV)
+    assert torch.all(big[M:] == 7.0)

@@ -27,7 +27,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 import numpy as np
@@ -124,53 +123,59 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU reference arm
-def cpu_reference_sample(budget_s=8.0):
-    """The reference's compute_gold (oracle/_ref) on this host's cores: returns
-    (weight GB/s, threads, sample description)."""
-    from oracle import api as orc
-    from ternocl_b200 import synth
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    rng = np.random.default_rng(0)
-    cases = []
-    for K, N in SHAPES:
-        A = synth.activations(rng, M, K, 0)
-        B = synth.pack_int2(synth.ternary(rng, K, N))
-        S = synth.scales(rng, K, N, 0)
-        cases.append((A, B, S, K, N))
-    use_ref = orc.ref_available()
-    gold = orc.Ref.int2_gold if use_ref else (lambda A, B, S, M_, K, N, bf: orc.int2_gold(A, B, S, M_, K, N, bf))
-    t0 = time.perf_counter()
-    steps, nbytes = 0, 0
-    while True:
-        for A, B, S, K, N in cases:
-            gold(A, B, S, M, K, N, 0)
-            nbytes += weight_bytes(K, N)
-        steps += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s:
-            break
-    return (nbytes / el / 1e9, threads, "reference" if use_ref else "port",
-            "%d passes over the 4 shapes (%.1f s, seed 0, M=1 fp16)" % (steps, el))
+class CpuReference:
+    """The reference's compute_gold (oracle/_ref: int2_fp16_upcvt/main.cpp:79-98 compiled
+    from the reference sources) on this host's cores, on the same workload; falls back
+    to the oracle's restatement ("port") where oracle/_ref is absent."""
+
+    def __init__(self):
+        from oracle import api as orc
+        from ternocl_b200 import synth
+        self.threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+        rng = np.random.default_rng(0)
+        self.cases = []
+        for K, N in SHAPES:
+            self.cases.append((synth.activations(rng, M, K, 0), synth.pack_int2(synth.ternary(rng, K, N)),
+                               synth.scales(rng, K, N, 0), K, N))
+        self.kind = "reference" if orc.ref_available() else "port"
+        self.gold = orc.Ref.int2_gold if self.kind == "reference" else orc.int2_gold
+
+    def one_pass(self):
+        """One step: one GEMV per shape. Returns seconds."""
+        t0 = time.perf_counter()
+        for A, B, S, K, N in self.cases:
+            self.gold(A, B, S, M, K, N, 0)
+        return time.perf_counter() - t0
+
+    def sample(self, budget_s=8.0):
+        """(weight GB/s, threads, kind, description) over a bounded number of passes."""
+        self.one_pass()
+        el, n = 0.0, 0
+        while el < budget_s:
+            el += self.one_pass()
+            n += 1
+        gb = n * sum(weight_bytes(K, N) for K, N in SHAPES) / 1e9
+        return gb / el, self.threads, self.kind, "%d passes over the 4 shapes, %.1f s, M=1 fp16, seed 0" % (n, el)
 
 
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    vals = []
-    desc = None
+    ref = CpuReference()
     for _ in range(args.warmup):
-        cpu_reference_sample(budget_s=0.5)
-    for _ in range(args.steps):
-        v, cores, kind, desc = cpu_reference_sample(budget_s=max(1.0, 20.0 / max(args.steps, 1)))
-        vals.append(v)
-    value = statistics.median(vals)
+        ref.one_pass()
+    # bounded: at most ~60 s of timed passes whatever --steps asks
+    t_pass = ref.one_pass()
+    n = max(1, min(args.steps, int(60.0 / max(t_pass, 1e-6))))
+    el = sum(ref.one_pass() for _ in range(n))
+    value = n * sum(weight_bytes(K, N) for K, N in SHAPES) / el / 1e9
+    desc = "%d of %d requested steps (one GEMV per shape each), %.1f s" % (n, args.steps, el)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": el / n * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic", "config": {"workload": WORKLOAD, "M": M, "shapes_KxN": SHAPES},
-            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": ref.threads, "kind": ref.kind,
                              "sample": desc},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -330,7 +335,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, kind, desc = cpu_reference_sample()
+        v, cores, kind, desc = CpuReference().sample()
         cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc}
 
     if rank == 0:

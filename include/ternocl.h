@@ -52,13 +52,24 @@ typedef enum {
 
 /* Kernel choice for the GEMM/GEMV families.  AUTO picks the decode GEMV for small
  * M and the tensor-core GEMM otherwise (the reference drivers switch at M >= 64,
- * int2_fp16_upcvt/main.cpp:160). */
-typedef enum { TERNOCL_ALGO_AUTO = 0, TERNOCL_ALGO_GEMV = 1, TERNOCL_ALGO_GEMM = 2 } ternocl_algo;
+ * int2_fp16_upcvt/main.cpp:160).  GEMV is the register-decode GEMV on warp-level
+ * MMAs; GEMV_TMEM the same contraction with the decoded weights in tensor memory and
+ * tcgen05.mma (a second, independent implementation, also used for cross-checks). */
+typedef enum {
+    TERNOCL_ALGO_AUTO = 0,
+    TERNOCL_ALGO_GEMV = 1,
+    TERNOCL_ALGO_GEMM = 2,
+    TERNOCL_ALGO_GEMV_TMEM = 3
+} ternocl_algo;
 
 const char *ternocl_version(void);
 const char *ternocl_status_string(int status);
 /* Last CUDA error string seen by this thread's ternocl calls ("" if none). */
 const char *ternocl_last_error(void);
+/* Device-side error word of the current device (synchronous read): bit 0 = a bounded
+ * wait inside a kernel gave up (the kernel returned without hanging; its outputs are
+ * invalid).  reset != 0 clears it.  Returns -1 if it cannot be read. */
+int ternocl_device_error(int reset);
 
 /* Process-wide options.
  *  TERNOCL_OPT_PDL (default 0): launch kernels with programmatic dependent launch,

@@ -11,7 +11,7 @@ from ._lib import LIB_PATH, TernoclError, call, header_functions, lib  # noqa: F
 
 FP16, BF16 = 0, 1
 POSTOP_NONE, POSTOP_SILU_MUL, POSTOP_ADD, POSTOP_BIAS, POSTOP_SIGMOID = range(5)
-ALGO_AUTO, ALGO_GEMV, ALGO_GEMM = 0, 1, 2
+ALGO_AUTO, ALGO_GEMV, ALGO_GEMM, ALGO_GEMV_TMEM = 0, 1, 2, 3
 OPT_PDL = 1
 
 
@@ -48,6 +48,11 @@ def _check_cuda(*ts):
 
 def set_option(option, value):
     return lib().ternocl_set_option(option, int(value))
+
+
+def device_error(reset=True):
+    """Device error word (bit 0: a bounded in-kernel wait timed out)."""
+    return lib().ternocl_device_error(int(bool(reset)))
 
 
 class Workspace:

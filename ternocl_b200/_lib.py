@@ -24,6 +24,7 @@ SIGNATURES = {
     "ternocl_status_string": (C.c_char_p, [i32]),
     "ternocl_last_error": (C.c_char_p, []),
     "ternocl_set_option": (i32, [i32, i32]),
+    "ternocl_device_error": (i32, [i32]),
     "ternocl_gemv_workspace_size": (sz, [i32, i32, i32]),
     "ternocl_int2_upcvt": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]),
     "ternocl_int1_upcvt": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]),

@@ -46,27 +46,54 @@ static bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 // GEMV split-K plan: enough CTAs (4 per SM) to keep every SM streaming.
 struct GemvPlan {
     int SK = 1;
+    bool cluster = false;  // 1 < SK <= 8: reduce through distributed shared memory
     size_t cnt_bytes = 0, part_bytes = 0;
-    size_t total() const { return SK > 1 ? cnt_bytes + part_bytes : 0; }
+    size_t total() const { return (SK > 1 && !cluster) ? cnt_bytes + part_bytes : 0; }
 };
 
 static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-static GemvPlan gemv_plan(int M, int N, int K, int sk_cap) {
+// shared memory a GEMV CTA may use (activation staging + weight ring)
+constexpr size_t kGemvSmemBudget = 100 * 1024;
+constexpr int kMaxClusterSK = 8;  // portable thread-block cluster size
+
+// Split-K plan of a decode GEMV whose CTAs cover `cols` columns x `rows` activation
+// rows: enough CTAs to give every SM `per_sm` of them, each CTA keeping >= 1 group
+// and its staged activations within the shared-memory budget.  Splits up to
+// `max_cluster` reduce through distributed shared memory; beyond that (only when a
+// workspace is available) through the workspace.
+template <class SmemFn>
+static GemvPlan gemv_plan_t(int M, int N, int K, int cols, int rows, int per_sm, int max_cluster,
+                            bool allow_ws, size_t smem_budget, SmemFn smem_of_sk) {
     GemvPlan p;
-    const int strips = (N + 31) / 32, zb = (M + 7) / 8, G = K / kGS;
+    const int strips = (N + cols - 1) / cols, zb = (M + rows - 1) / rows, G = K / kGS;
     const long long tiles = (long long)strips * zb;
-    const long long target = 4LL * sm_count();
+    const long long target = (long long)per_sm * sm_count();
     int sk = (int)((target + tiles - 1) / tiles);
-    const int max_sk = G / 4 > 1 ? G / 4 : 1;  // >= 4 groups (one per warp) per CTA
-    if (sk > max_sk) sk = max_sk;
-    if (sk > 16) sk = 16;
-    if (sk > sk_cap) sk = sk_cap;
+    if (sk > G) sk = G;
+    if (sk > 32) sk = 32;
+    while (sk < G && smem_of_sk(sk) > smem_budget) ++sk;
+    if (sk > max_cluster && !allow_ws) sk = max_cluster;
     if (sk < 1) sk = 1;
     p.SK = sk;
+    p.cluster = sk > 1 && sk <= max_cluster;
     p.cnt_bytes = round_up((size_t)tiles * sizeof(unsigned), 256);
     p.part_bytes = (size_t)sk * M * N * sizeof(float);
     return p;
+}
+
+// warp-level mma.sync GEMV (gemv_int2.cu): 32 columns x 8 rows per CTA
+static GemvPlan gemv_plan(int M, int N, int K, bool allow_ws) {
+    return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
+                       [&](int sk) { return int2_gemv_smem(M, K, sk); });
+}
+
+// tcgen05 GEMV (gemv_tc.cu): 128 columns x tc_gemv_rows(M) rows per CTA, 4 CTAs/SM
+// (each holds 128 of the SM's 512 TMEM columns; <= 52 KB of shared memory keeps 4
+// of them resident)
+static GemvPlan gemv_tc_plan(int M, int N, int K, bool allow_ws) {
+    return gemv_plan_t(M, N, K, 128, tc_gemv_rows(M), 4, 16, allow_ws, 52 * 1024,
+                       [&](int sk) { return int2_gemv_tc_smem(M, K, sk); });
 }
 
 static int check_gemm_common(const void *A, const void *B, const void *S, const void *C,
@@ -121,7 +148,15 @@ int ternocl_set_option(int option, int value) {
 
 size_t ternocl_gemv_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0 || N % 16 || K % kGS) return 0;
-    return gemv_plan(M, N, K, 1 << 30).total();
+    const size_t a = gemv_plan(M, N, K, true).total(), b = gemv_tc_plan(M, N, K, true).total();
+    return a > b ? a : b;
+}
+
+int ternocl_device_error(int reset) {
+    unsigned v = 0, t = 0;
+    if (read_device_error_gemv_tc(&t, reset) != cudaSuccess) return -1;
+    v |= t;
+    return (int)v;
 }
 
 int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,
@@ -129,21 +164,26 @@ int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
                        int algo, void *ws, size_t ws_bytes, void *stream) {
     int st = check_gemm_common(A, B, S, C, Other, Bias, M, N, K, dtype, postop, out_f32);
     if (st != TERNOCL_OK) return st;
-    if (algo < TERNOCL_ALGO_AUTO || algo > TERNOCL_ALGO_GEMM) return TERNOCL_ERR_ARG;
+    if (algo < TERNOCL_ALGO_AUTO || algo > TERNOCL_ALGO_GEMV_TMEM) return TERNOCL_ERR_ARG;
     if (M == 0) return TERNOCL_OK;
     GemvArgs a;
     a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.stream = (cudaStream_t)stream;
     // (the tensor-core GEMM path is selected for large M once available)
-    GemvPlan p = gemv_plan(M, N, K, ws ? 1 << 30 : 1);
-    while (p.SK > 1 && (!ws || p.total() > ws_bytes)) p = gemv_plan(M, N, K, p.SK - 1);
-    if (p.SK > 1) {
+    const bool simt = algo != TERNOCL_ALGO_GEMV_TMEM;
+    GemvPlan p = simt ? gemv_plan(M, N, K, ws != nullptr) : gemv_tc_plan(M, N, K, ws != nullptr);
+    if (p.total() > ws_bytes) p = simt ? gemv_plan(M, N, K, false) : gemv_tc_plan(M, N, K, false);
+    const size_t smem = simt ? int2_gemv_smem(M, K, p.SK) : int2_gemv_tc_smem(M, K, p.SK);
+    if (smem > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    a.SK = p.SK;
+    a.cluster = p.cluster ? 1 : 0;
+    if (p.total() > 0) {
         if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
-        a.SK = p.SK;
         a.ws_cnt = (unsigned *)ws;
         a.ws_part = (float *)((char *)ws + p.cnt_bytes);
     }
+    if (!simt) return cuda_status(int2_gemv_tc_launch(a));
     return cuda_status(int2_gemv_launch(a));
 }
 

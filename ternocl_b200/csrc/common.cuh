@@ -179,26 +179,21 @@ struct Int2Decode<BF16> {
 };
 
 // ---------------------------------------------------------------------------------
-// Warp-level tensor-core MMA m16n8k16, fp32 accumulate (A row-major 16x16, B
-// column-major 16x8).  Used by the decode GEMVs, whose operands are built in
+// Warp-level tensor-core MMA m16n8k16, fp32 accumulate in place (A row-major 16x16,
+// B column-major 16x8).  Used by the decode GEMVs, whose operands are built in
 // registers (the weights are the 16-row operand, activation rows the 8 columns).
 template <class DT>
-__device__ __forceinline__ void mma16816(float d[4], const uint32_t a[4], const uint32_t b[2],
-                                         const float c[4]) {
+__device__ __forceinline__ void mma16816(float d[4], const uint32_t a[4], const uint32_t b[2]) {
     if constexpr (DT::kBF16) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-            "{%8,%9}, {%10,%11,%12,%13};\n"
-            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(c[0]),
-              "f"(c[1]), "f"(c[2]), "f"(c[3]));
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
     } else {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-            "{%8,%9}, {%10,%11,%12,%13};\n"
-            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(c[0]),
-              "f"(c[1]), "f"(c[2]), "f"(c[3]));
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
     }
 }
 

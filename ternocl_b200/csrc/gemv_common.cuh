@@ -1,0 +1,285 @@
+// Skeleton shared by the decode GEMVs (int2 / s8xs2 / int1 / BITCOS): CTA work
+// split, cp.async weight ring, activation staging, deterministic split-K reduction
+// and the fused epilogue store.  A Policy supplies the weight layout specifics.
+//
+// Work decomposition.  A CTA (4 warps) owns a strip of 32 output columns, 8
+// activation rows (grid.z) and a contiguous range of 128-row scale groups
+// (grid.y = SK cross-CTA K split); its 4 warps split that range again.  Thread
+// (g = lane/4, q = lane%4) owns the MMA fragment rows g and g+8 of the strip's two
+// 16-column blocks (4 output columns) and activation row g of the 8.
+//
+// Memory pipeline.  Each thread streams ITS OWN weight bytes of every group (the
+// policy says which) through a kStages-deep cp.async ring in shared memory, so the
+// bytes in flight cost no registers; the copies for the first stages are issued
+// before griddepcontrol.wait (programmatic dependent launch), i.e. they overlap the
+// previous kernel in the stream.  Activations are staged once per CTA, already
+// permuted into the MMA fragment order, after that wait.
+//
+// Determinism.  The 4 warps are reduced in warp order through shared memory.  With
+// 1 < SK <= 8 the SK CTAs of a strip form a thread-block cluster: each leaves its
+// fp32 partial in its shared memory and cluster rank 0 sums them over distributed
+// shared memory in split order.  With SK > 8 each CTA writes its partial tile to a
+// global workspace, and the last CTA to arrive for the tile (atomic counter, no
+// waiting) sums the SK partials in split order and resets the counter.  Either way
+// the summation order is fixed, so results are bitwise reproducible.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace ternocl {
+namespace gemv {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 4;
+constexpr int kActPadBytes = 16;
+
+struct Params {
+    const uint16_t *A;
+    const uint32_t *B;
+    const uint16_t *S;
+    const uint32_t *SR;  // BITCOS slice ranks (unused by the other layouts)
+    void *C;
+    const uint16_t *Other;
+    const void *Bias;
+    int M, N, K, SK;
+    int cluster;  // 1: the SK CTAs of a strip form one thread-block cluster (SK <= 8)
+    float *ws_part;
+    unsigned *ws_cnt;
+};
+
+// Thread-block cluster helpers (distributed shared memory).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src));
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(dst)), "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Per-thread ring slot of one stage: Policy::kWords16 16-byte weight chunks + one
+// 8-byte scale chunk, laid out [chunk][thread] so a warp's accesses are contiguous.
+template <class Policy>
+struct Ring {
+    static constexpr int kStageBytes = (Policy::kWords16 * 16 + 8) * kThreads;
+    static constexpr int kBytes = kStages * kStageBytes;
+    __device__ static uint4 *words(char *base, int stage, int c, int tid) {
+        return reinterpret_cast<uint4 *>(base + stage * kStageBytes + (c * kThreads + tid) * 16);
+    }
+    __device__ static uint2 *scale(char *base, int stage, int tid) {
+        return reinterpret_cast<uint2 *>(base + stage * kStageBytes + Policy::kWords16 * 16 * kThreads + tid * 8);
+    }
+};
+
+// Bytes of dynamic shared memory for a CTA that stages `krange` activation rows'
+// worth of K (rows = 8 activation rows).
+template <class Policy>
+__host__ __device__ inline size_t smem_bytes(int rows, int krange) {
+    const size_t act = (size_t)rows * ((size_t)krange * 2 + kActPadBytes);
+    const size_t red = (size_t)kWarps * 32 * 8 * sizeof(float);  // warp partials + CTA partial
+    const size_t ring = Ring<Policy>::kBytes;
+    return (ring > red ? ring : red) + act + Policy::extra_smem(rows, krange);
+}
+
+template <class Policy, class DT, int POSTOP, bool OUT_F32>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
+    extern __shared__ __align__(128) char smem[];
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, q = lane & 3;
+    const int n0 = blockIdx.x * 32;
+    const int mb = blockIdx.z * 8;
+    const int G = p.K / kGS;
+    const int sk = blockIdx.y;
+    const int cg0 = (int)((long long)G * sk / p.SK), cg1 = (int)((long long)G * (sk + 1) / p.SK);
+    const int ng = cg1 - cg0;
+    const int wg0 = cg0 + ng * warp / kWarps, wg1 = cg0 + ng * (warp + 1) / kWarps;
+    const int rows = min(8, p.M - mb);
+    const int krange = ng * kGS;
+    const bool colok = n0 + Policy::thread_col0(g) < p.N;  // N % 16 == 0
+
+    char *ring = smem;
+    char *act = smem + (Ring<Policy>::kBytes > kWarps * 32 * 8 * 4 ? Ring<Policy>::kBytes : kWarps * 32 * 8 * 4);
+    const int act_stride = krange * 2 + kActPadBytes;  // bytes per staged activation row
+    char *extra = act + (size_t)rows * act_stride;
+
+    // weight stream of this warp's groups [wg0, wg1): pointers advance by one group per issue
+    const int nwg = wg1 - wg0;
+    const uint32_t *wsrc = Policy::word_ptr(p, wg0, g, q, n0);
+    const uint16_t *ssrc = p.S + (size_t)wg0 * p.N + n0 + Policy::thread_col0(g);
+    const size_t wstride = Policy::group_stride(p), cstride = Policy::chunk_stride(p);
+    int issued = 0;
+    auto issue = [&]() {
+        if (issued < nwg && colok) {
+            const int stage = issued & (kStages - 1);
+#pragma unroll
+            for (int c = 0; c < Policy::kWords16; ++c)
+                cp_async16(Ring<Policy>::words(ring, stage, c, tid), wsrc + c * cstride);
+            cp_async8(Ring<Policy>::scale(ring, stage, tid), ssrc);
+        }
+        cp_async_commit();
+        wsrc += wstride;
+        ssrc += p.N;
+        ++issued;
+    };
+    static_assert((kStages & (kStages - 1)) == 0, "ring depth must be a power of two");
+
+#pragma unroll
+    for (int i = 0; i < kStages - 1; ++i) issue();
+    pdl_wait();
+    Policy::template stage<DT>(p, act, act_stride, extra, mb, rows, cg0, ng);
+    __syncthreads();
+
+    float acc[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+
+    const bool rowok = g < rows;
+    const char *arow = act + (size_t)(rowok ? g : 0) * act_stride + (size_t)(wg0 - cg0) * Policy::kActGroupBytes;
+    const char *xg = extra + (size_t)(wg0 - cg0) * Policy::kExtraGroupBytes;
+    for (int i = 0; i < nwg; ++i) {
+        cp_async_wait<kStages - 2>();
+        const int stage = i & (kStages - 1);
+        uint4 w[Policy::kWords16];
+#pragma unroll
+        for (int c = 0; c < Policy::kWords16; ++c) w[c] = *Ring<Policy>::words(ring, stage, c, tid);
+        const uint2 sc = *Ring<Policy>::scale(ring, stage, tid);
+        Policy::template compute<DT>(w, sc, arow, rowok, q, xg, acc, g);
+        arow += Policy::kActGroupBytes;
+        xg += Policy::kExtraGroupBytes;
+        issue();
+    }
+    cp_async_wait<0>();
+    pdl_launch_dependents();
+
+    // in-CTA reduction over the K-split warps, in warp order (ring memory reused)
+    float v[8];
+    Policy::thread_values(acc, v);  // v[h*4 + i]: activation row mb+2q+h, column col(i)
+    __syncthreads();
+    float(*red)[32][8] = reinterpret_cast<float(*)[32][8]>(smem);  // [kWarps][lane][8]
+    if (warp > 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) red[warp - 1][lane][i] = v[i];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int w = 0; w < kWarps - 1; ++w)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] += red[w][lane][i];
+    }
+
+    int cols[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) cols[i] = n0 + Policy::thread_col(g, i);
+
+    auto store = [&]() {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = mb + 2 * q + h;
+            if (m < p.M) {
+                if (Policy::kContiguousCols) {
+                    epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[0], v[4 * h], v[4 * h + 1]);
+                    epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[2], v[4 * h + 2], v[4 * h + 3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        epi_store<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[i], v[4 * h + i]);
+                }
+            }
+        }
+    };
+
+    if (p.SK == 1) {
+        if (warp == 0 && colok) store();
+        return;
+    }
+    if (p.cluster) {
+        // split-K across the CTAs of a cluster: partials through distributed shared
+        // memory, summed by cluster rank 0 in rank (= K split) order
+        float *mine = &red[kWarps - 1][lane][0];
+        if (warp == 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mine[i] = v[i];
+        }
+        cluster_sync_all();
+        if (cluster_ctarank() == 0 && warp == 0) {
+            const uint32_t la = smem_u32(mine);
+            for (int r = 1; r < p.SK; ++r) {
+                const float4 x0 = ld_dsmem_f4(la, (uint32_t)r);
+                const float4 x1 = ld_dsmem_f4(la + 16, (uint32_t)r);
+                v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+                v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+            }
+            if (colok) store();
+        }
+        cluster_sync_all();  // keep every CTA's partial alive until rank 0 has read it
+        return;
+    }
+    if (warp != 0) return;
+    if (colok) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = mb + 2 * q + h;
+            if (m < p.M) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) __stcg(p.ws_part + ((size_t)sk * p.M + m) * p.N + cols[i], v[4 * h + i]);
+            }
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    const unsigned tile = blockIdx.z * gridDim.x + blockIdx.x;
+    unsigned last = 0;
+    if (lane == 0) last = (atomicAdd(&p.ws_cnt[tile], 1u) == (unsigned)(p.SK - 1)) ? 1u : 0u;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    if (colok) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = mb + 2 * q + h;
+            if (m < p.M) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float t = 0.0f;
+                    for (int s = 0; s < p.SK; ++s) t += __ldcg(p.ws_part + ((size_t)s * p.M + m) * p.N + cols[i]);
+                    v[4 * h + i] = t;
+                }
+            }
+        }
+        store();
+    }
+    if (lane == 0) p.ws_cnt[tile] = 0u;  // ready for the next call
+}
+
+}  // namespace gemv
+}  // namespace ternocl

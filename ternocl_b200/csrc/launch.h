@@ -30,6 +30,7 @@ struct GemvArgs {
     int M = 0, N = 0, K = 0;
     int dtype = 0, postop = 0, out_f32 = 0;
     int SK = 1;                  // cross-CTA K split
+    int cluster = 0;             // SK CTAs per thread-block cluster (DSMEM reduction)
     float *ws_part = nullptr;    // [SK][M][N] fp32 partials
     unsigned *ws_cnt = nullptr;  // per-tile arrival counters
     cudaStream_t stream = nullptr;
@@ -62,22 +63,46 @@ cudaError_t dispatch_epilogue(const Args &a, F &&f) {
 }
 
 template <class... KArgs, class... Args>
-cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                          cudaStream_t stream, Args &&...args) {
+cudaError_t launch_kernel_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t stream, dim3 cluster, Args &&...args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (options().pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (cluster.x * cluster.y * cluster.z > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster.x;
+        attr[n].val.clusterDim.y = cluster.y;
+        attr[n].val.clusterDim.z = cluster.z;
+        ++n;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = options().pdl ? 1 : 0;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <class... KArgs, class... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args &&...args) {
+    return launch_kernel_cluster(kernel, grid, block, smem, stream, dim3(1, 1, 1),
+                                 std::forward<Args>(args)...);
 }
 
 // Kernel-family entry points (one per .cu file).
 cudaError_t int2_gemv_launch(const GemvArgs &a);
+size_t int2_gemv_smem(int M, int K, int SK);
+// tcgen05 / TMEM decode GEMV (gemv_tc.cu): 128 columns and tc_gemv_rows(M) rows per CTA
+int tc_gemv_rows(int M);
+size_t int2_gemv_tc_smem(int M, int K, int SK);
+cudaError_t int2_gemv_tc_launch(const GemvArgs &a);
+cudaError_t read_device_error_gemv_tc(unsigned *out, int reset);
 
 }  // namespace ternocl

@@ -25,36 +25,54 @@ def run(tl, c, M, K, N, bf16, postop, out_f32, algo, ws=None):
     return host_dt(out)
 
 
+ALGOS = [1, 3]  # register-decode mma.sync GEMV, tcgen05/TMEM GEMV
+
+
+@pytest.mark.parametrize("algo", ALGOS)
 @pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("M,K,N", GEMV_SHAPES)
-def test_gemv_parity(cuda, tl, M, K, N, bf16):
+def test_gemv_parity(cuda, tl, M, K, N, bf16, algo):
     c = int2_case(100 + M + K + N, M, K, N, bf16)
     gold = int2_gold_out(c, M, K, N, bf16, 0, False)
     ws = tl.Workspace()
     for w in (None, ws):
-        out = run(tl, c, M, K, N, bf16, 0, False, tl.ALGO_GEMV, w)
-        check_output(out, gold, bf16, False, "int2 gemv M=%d K=%d N=%d bf16=%d" % (M, K, N, bf16))
+        out = run(tl, c, M, K, N, bf16, 0, False, algo, w)
+        check_output(out, gold, bf16, False, "int2 gemv algo=%d M=%d K=%d N=%d bf16=%d" % (algo, M, K, N, bf16))
+    assert tl.device_error() == 0
 
 
+@pytest.mark.parametrize("algo", ALGOS)
 @pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("postop", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("out_f32", [False, True])
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 512), (3, 2048, 1024)])
-def test_gemv_epilogues(cuda, tl, M, K, N, bf16, postop, out_f32):
+def test_gemv_epilogues(cuda, tl, M, K, N, bf16, postop, out_f32, algo):
     # validate_epilogues.sh:19-39: every POSTOP x {DT, fp32 out} x dtype
     c = int2_case(7 * postop + M, M, K, N, bf16, postop, out_f32)
     gold = int2_gold_out(c, M, K, N, bf16, postop, out_f32)
-    out = run(tl, c, M, K, N, bf16, postop, out_f32, tl.ALGO_GEMV, tl.Workspace())
+    out = run(tl, c, M, K, N, bf16, postop, out_f32, algo, tl.Workspace())
     check_output(out, gold, bf16, out_f32, "postop=%d out_f32=%d" % (postop, out_f32))
 
 
-def test_gemv_deterministic(cuda, tl):
+@pytest.mark.parametrize("algo", ALGOS)
+def test_gemv_deterministic(cuda, tl, algo):
     # main.cpp:351-353: every set reproduces set 0 bit for bit
     M, K, N = 4, 4096, 2048
     c = int2_case(5, M, K, N, 0)
     ws = tl.Workspace()
-    outs = [run(tl, c, M, K, N, 0, 0, False, tl.ALGO_GEMV, ws) for _ in range(3)]
+    outs = [run(tl, c, M, K, N, 0, 0, False, algo, ws) for _ in range(3)]
     assert all(np.array_equal(outs[0], o) for o in outs[1:])
+
+
+@pytest.mark.parametrize("M", [1, 2, 5, 8, 13, 16, 17, 40])
+def test_tc_gemv_row_blocks(cuda, tl, M):
+    # every activation-row block size of the TMEM GEMV (1, 2, 4, 8, 16 rows per CTA)
+    K, N = 1024, 384
+    c = int2_case(300 + M, M, K, N, 1)
+    gold = int2_gold_out(c, M, K, N, 1, 0, False)
+    out = run(tl, c, M, K, N, 1, 0, False, tl.ALGO_GEMV_TMEM, tl.Workspace())
+    check_output(out, gold, 1, False, "tc gemv M=%d" % M)
+    assert tl.device_error() == 0
 
 
 def test_gemv_ragged_rows_untouched(cuda, tl):

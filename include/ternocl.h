@@ -102,6 +102,24 @@ int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
                        const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,
                        int algo, void *ws, size_t ws_bytes, void *stream);
 
+/* Allocation-free int2 decode GEMV (no counterpart in the reference: its OpenCL
+ * drivers always allocate their buffers).  For callers that cannot allocate device
+ * memory where they run -- inside another framework's memory pool, in runtimes that
+ * forbid allocation after start-up, in plugins whose host owns all allocations --
+ * this computes the same C as ternocl_int2_upcvt (same arguments and rules, no
+ * workspace argument) and takes its split-K scratch from a 16 MiB array the library
+ * declares in device memory, which every GPU that loads the library holds until exit.
+ *  - Shapes whose scratch (2 x M x N fp32 partial sums + counters) exceeds 16 MiB
+ *    are rejected with TERNOCL_ERR_WORKSPACE.
+ *  - The first call on a device looks up the array's address (cudaGetSymbolAddress,
+ *    that device current); make that first call before any stream capture.
+ *  - All calls share the array: the counters are cleared on `stream` before each
+ *    launch; calls that overlap on the GPU race on it.
+ *  - Calls no cudaMalloc, cudaFree or allocating library routine. */
+int ternocl_int2_upcvt_noalloc(const void *A, const uint32_t *B, const void *S, void *C,
+                               const void *Other, const void *Bias, int M, int N, int K, int dtype,
+                               int postop, int out_f32, void *stream);
+
 /* ---------------------------------------------------------------------------------
  * int1 (binary) upconvert GEMM/GEMV.  Replaces int1_fp16_upcvt_gemm / _gemm_mt
  * (int1_fp16_upcvt.cl:166-170, 302-306).  B is the device "sel" layout, uint32

@@ -27,6 +27,7 @@ SIGNATURES = {
     "ternocl_device_error": (i32, [i32]),
     "ternocl_gemv_workspace_size": (sz, [i32, i32, i32]),
     "ternocl_int2_upcvt": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]),
+    "ternocl_int2_upcvt_noalloc": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
     "ternocl_int1_upcvt": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]),
     "ternocl_int8_ldsa": (i32, [i32]),
     "ternocl_int8_quant_a": (i32, [vp, vp, vp, i32, i32, i32, vp]),

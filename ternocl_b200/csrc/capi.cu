@@ -113,6 +113,9 @@ static int check_gemm_common(const void *A, const void *B, const void *S, const 
     return TERNOCL_OK;
 }
 
+int gemv_split_k(int M, int N, int K) { return gemv_plan(M, N, K, true).SK; }
+int report_cuda(cudaError_t e) { return cuda_status(e); }
+
 }  // namespace ternocl
 
 using namespace ternocl;

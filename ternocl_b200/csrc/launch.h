@@ -104,5 +104,9 @@ int tc_gemv_rows(int M);
 size_t int2_gemv_tc_smem(int M, int K, int SK);
 cudaError_t int2_gemv_tc_launch(const GemvArgs &a);
 cudaError_t read_device_error_gemv_tc(unsigned *out, int reset);
+// split-K factor the register-decode GEMV's planner picks when a workspace exists
+int gemv_split_k(int M, int N, int K);
+// CUDA error -> ternocl status (records ternocl_last_error)
+int report_cuda(cudaError_t e);
 
 }  // namespace ternocl

@@ -116,3 +116,47 @@ def int1_upcvt(A, B, S, postop=0, out_f32=False, other=None, bias=None, out=None
     """C = epi(A @ dequant_int1(B, S)); B int32 [K/32,N] in the device sel layout."""
     return _upcvt("ternocl_int1_upcvt", A, B, S, postop, out_f32, other, bias, out, algo,
                   workspace, stream)
+
+
+def int8_ldsa(M):
+    """Row pitch of SA (elements): (M + 31) & ~31, as LDSA() of the reference kernel."""
+    return lib().ternocl_int8_ldsa(M)
+
+
+def int8_quant_a(A, write_q=True, stream=None):
+    """Per-(row, 128-group) activation scales SA [K/128, ldsa(M)] (dtype of A) and, with
+    write_q, the int8 codes Aq [M, K].  Returns (SA, Aq or None)."""
+    torch = _torch()
+    _check_cuda(A)
+    M, K = A.shape
+    SA = torch.zeros(K // 128, int8_ldsa(M), dtype=A.dtype, device=A.device)
+    Aq = torch.empty(M, K, dtype=torch.int8, device=A.device) if write_q else None
+    call("ternocl_int8_quant_a", _ptr(A), _ptr(SA), _ptr(Aq), M, K, dtype_code(A), _stream(stream))
+    return SA, Aq
+
+
+def int2_int8(A, B, SB, SA, Aq=None, qmode=None, postop=0, out_f32=False, other=None, bias=None,
+              out=None, algo=0, stream=None):
+    """s8 x s2: C = epi(sum_g float(int32 dot_g) * (SB * 1/SA)).  qmode 0 reads Aq
+    (from int8_quant_a), qmode 1 quantises A in the kernel; default: 0 if Aq is given."""
+    _check_cuda(A, B, SB, SA, Aq, other, bias, out)
+    if qmode is None:
+        qmode = 0 if Aq is not None else 1
+    M, K = A.shape
+    N = B.shape[1]
+    C = _out(M, N, A, out_f32, out)
+    call("ternocl_int2_int8", _ptr(A), _ptr(Aq), _ptr(SA), _ptr(B), _ptr(SB), _ptr(C), _ptr(other),
+         _ptr(bias), M, N, K, dtype_code(A), int(postop), int(bool(out_f32)), int(qmode), int(algo),
+         _stream(stream))
+    return C
+
+
+def int2_int8_group_dots(Aq, B, stream=None):
+    """int32 Dots [M, K/128, N] = per-group sum of Aq[m, k] * code(B[k, n])."""
+    torch = _torch()
+    _check_cuda(Aq, B)
+    M, K = Aq.shape
+    N = B.shape[1]
+    D = torch.empty(M, K // 128, N, dtype=torch.int32, device=Aq.device)
+    call("ternocl_int2_int8_group_dots", _ptr(Aq), _ptr(B), _ptr(D), M, N, K, _stream(stream))
+    return D

@@ -88,6 +88,18 @@ static GemvPlan gemv_plan(int M, int N, int K, bool allow_ws) {
                        [&](int sk) { return int2_gemv_smem(M, K, sk); });
 }
 
+// int1 GEMV (gemv_int1.cu): same CTA shape
+static GemvPlan gemv_i1_plan(int M, int N, int K, bool allow_ws) {
+    return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
+                       [&](int sk) { return int1_gemv_smem(M, K, sk); });
+}
+
+// s8 x s2 GEMV (gemv_int8.cu): same CTA shape, int8 activation staging
+static GemvPlan gemv_i8_plan(int M, int N, int K, bool allow_ws) {
+    return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
+                       [&](int sk) { return int8_gemv_smem(M, K, sk); });
+}
+
 // tcgen05 GEMV (gemv_tc.cu): 128 columns x tc_gemv_rows(M) rows per CTA, 4 CTAs/SM
 // (each holds 128 of the SM's 512 TMEM columns; <= 52 KB of shared memory keeps 4
 // of them resident)
@@ -151,8 +163,12 @@ int ternocl_set_option(int option, int value) {
 
 size_t ternocl_gemv_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0 || N % 16 || K % kGS) return 0;
-    const size_t a = gemv_plan(M, N, K, true).total(), b = gemv_tc_plan(M, N, K, true).total();
-    return a > b ? a : b;
+    // the largest need of the GEMVs that take a workspace (int2 on either path, int1)
+    size_t need = gemv_plan(M, N, K, true).total();
+    const size_t b = gemv_tc_plan(M, N, K, true).total(), c = gemv_i1_plan(M, N, K, true).total();
+    if (b > need) need = b;
+    if (c > need) need = c;
+    return need;
 }
 
 int ternocl_device_error(int reset) {
@@ -190,23 +206,73 @@ int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
     return cuda_status(int2_gemv_launch(a));
 }
 
-// ---- entry points whose kernels are not built yet: report UNSUPPORTED ----------
-int ternocl_int1_upcvt(const void *, const uint32_t *, const void *, void *, const void *,
-                       const void *, int, int, int, int, int, int, int, void *, size_t, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+int ternocl_int1_upcvt(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,
+                       const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,
+                       int algo, void *ws, size_t ws_bytes, void *stream) {
+    int st = check_gemm_common(A, B, S, C, Other, Bias, M, N, K, dtype, postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (algo < TERNOCL_ALGO_AUTO || algo > TERNOCL_ALGO_GEMM) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    GemvArgs a;
+    a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
+    a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.stream = (cudaStream_t)stream;
+    GemvPlan p = gemv_i1_plan(M, N, K, ws != nullptr);
+    if (p.total() > ws_bytes) p = gemv_i1_plan(M, N, K, false);
+    if (int1_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    a.SK = p.SK;
+    a.cluster = p.cluster ? 1 : 0;
+    if (p.total() > 0) {
+        if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
+        a.ws_cnt = (unsigned *)ws;
+        a.ws_part = (float *)((char *)ws + p.cnt_bytes);
+    }
+    return cuda_status(int1_gemv_launch(a));
 }
+
 int ternocl_int8_ldsa(int M) { return (M + 31) & ~31; }
-int ternocl_int8_quant_a(const void *, void *, int8_t *, int, int, int, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+
+int ternocl_int8_quant_a(const void *A, void *SA, int8_t *Aq, int M, int K, int dtype, void *stream) {
+    if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
+    if (M < 0 || K <= 0 || K % kGS) return TERNOCL_ERR_SHAPE;
+    if (!A || !SA) return TERNOCL_ERR_ARG;
+    if (!aligned(A, 8) || !aligned(SA, 2) || (Aq && !aligned(Aq, 4))) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    return cuda_status(quant_a_launch(A, SA, Aq, M, K, dtype, (cudaStream_t)stream));
 }
-int ternocl_int2_int8(const void *, const int8_t *, const void *, const uint32_t *, const void *,
-                      void *, const void *, const void *, int, int, int, int, int, int, int, int,
-                      void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+
+int ternocl_int2_int8(const void *A, const int8_t *Aq, const void *SA, const uint32_t *B,
+                      const void *SB, void *C, const void *Other, const void *Bias, int M, int N,
+                      int K, int dtype, int postop, int out_f32, int qmode, int algo, void *stream) {
+    if (qmode != 0 && qmode != 1) return TERNOCL_ERR_ARG;
+    const void *act = qmode == 0 ? (const void *)Aq : A;  // the operand the kernel reads
+    int st = check_gemm_common(act, B, SB, C, Other, Bias, M, N, K, dtype, postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (!SA || !aligned(SA, 2)) return TERNOCL_ERR_ARG;
+    if (algo != TERNOCL_ALGO_AUTO && algo != TERNOCL_ALGO_GEMV) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    GemvArgs a;
+    a.A = A; a.B = B; a.S = SB; a.C = C; a.Other = Other; a.Bias = Bias;
+    a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.Aq = Aq; a.SA = SA; a.qmode = qmode;
+    a.stream = (cudaStream_t)stream;
+    // no workspace in this signature: split-K stays within one thread-block cluster
+    const GemvPlan p = gemv_i8_plan(M, N, K, false);
+    if (int8_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    a.SK = p.SK;
+    a.cluster = p.cluster ? 1 : 0;
+    return cuda_status(int8_gemv_launch(a));
 }
-int ternocl_int2_int8_group_dots(const int8_t *, const uint32_t *, int32_t *, int, int, int, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+
+int ternocl_int2_int8_group_dots(const int8_t *Aq, const uint32_t *B, int32_t *Dots, int M, int N,
+                                 int K, void *stream) {
+    if (M < 0 || N <= 0 || K <= 0 || N % 16 || K % kGS) return TERNOCL_ERR_SHAPE;
+    if (!Aq || !B || !Dots) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    return cuda_status(group_dots_launch(Aq, B, Dots, M, N, K, (cudaStream_t)stream));
 }
+
+// ---- entry points whose kernels are not built yet: report UNSUPPORTED ----------
 int ternocl_bitcos_upcvt(const void *, const uint32_t *, const void *, const uint32_t *, int, void *,
                          const void *, const void *, int, int, int, int, int, int, int, void *) {
     return TERNOCL_ERR_UNSUPPORTED;

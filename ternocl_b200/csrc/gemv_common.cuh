@@ -33,7 +33,6 @@ namespace gemv {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 4;
-constexpr int kActPadBytes = 16;
 
 struct Params {
     const uint16_t *A;
@@ -47,6 +46,10 @@ struct Params {
     int cluster;  // 1: the SK CTAs of a strip form one thread-block cluster (SK <= 8)
     float *ws_part;
     unsigned *ws_cnt;
+    // s8 x s2: int8 activations (qmode 0) and activation scales SA [K/128, ldsa]
+    const int8_t *Aq;
+    const uint16_t *SA;
+    int ldsa, qmode;
 };
 
 // Thread-block cluster helpers (distributed shared memory).
@@ -68,6 +71,37 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local_addr, uint32_t rank
     return v;
 }
 
+}  // namespace gemv
+}  // namespace ternocl
+
+#include "launch.h"
+
+namespace ternocl {
+namespace gemv {
+
+inline Params gemv_params_impl(const GemvArgs &a) {
+    Params p{};
+    p.A = (const uint16_t *)a.A;
+    p.B = a.B;
+    p.S = (const uint16_t *)a.S;
+    p.SR = nullptr;
+    p.C = a.C;
+    p.Other = (const uint16_t *)a.Other;
+    p.Bias = a.Bias;
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    p.SK = a.SK;
+    p.cluster = a.cluster;
+    p.ws_part = a.ws_part;
+    p.ws_cnt = a.ws_cnt;
+    p.Aq = a.Aq;
+    p.SA = (const uint16_t *)a.SA;
+    p.ldsa = (a.M + 31) & ~31;
+    p.qmode = a.qmode;
+    return p;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -85,6 +119,8 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // Per-thread ring slot of one stage: Policy::kWords16 16-byte weight chunks + one
 // 8-byte scale chunk, laid out [chunk][thread] so a warp's accesses are contiguous.
+// Policy::read_words hands compute() its kWordRegs 16-byte registers from a stage:
+// its own chunks, or (kSharedSlots) chunks copied by other lanes of its warp.
 template <class Policy>
 struct Ring {
     static constexpr int kStageBytes = (Policy::kWords16 * 16 + 8) * kThreads;
@@ -97,11 +133,18 @@ struct Ring {
     }
 };
 
-// Bytes of dynamic shared memory for a CTA that stages `krange` activation rows'
-// worth of K (rows = 8 activation rows).
+// Bytes per staged activation row: Policy::kActBytesPerK per K element plus a pad
+// that staggers the rows across shared-memory banks.
+template <class Policy>
+__host__ __device__ inline int act_row_bytes(int krange) {
+    return krange * Policy::kActBytesPerK + Policy::kActPadBytes;
+}
+
+// Bytes of dynamic shared memory for a CTA that stages `krange` K elements of
+// `rows` (<= 8) activation rows.
 template <class Policy>
 __host__ __device__ inline size_t smem_bytes(int rows, int krange) {
-    const size_t act = (size_t)rows * ((size_t)krange * 2 + kActPadBytes);
+    const size_t act = (size_t)rows * act_row_bytes<Policy>(krange);
     const size_t red = (size_t)kWarps * 32 * 8 * sizeof(float);  // warp partials + CTA partial
     const size_t ring = Ring<Policy>::kBytes;
     return (ring > red ? ring : red) + act + Policy::extra_smem(rows, krange);
@@ -126,7 +169,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
 
     char *ring = smem;
     char *act = smem + (Ring<Policy>::kBytes > kWarps * 32 * 8 * 4 ? Ring<Policy>::kBytes : kWarps * 32 * 8 * 4);
-    const int act_stride = krange * 2 + kActPadBytes;  // bytes per staged activation row
+    const int act_stride = act_row_bytes<Policy>(krange);
     char *extra = act + (size_t)rows * act_stride;
 
     // weight stream of this warp's groups [wg0, wg1): pointers advance by one group per issue
@@ -135,13 +178,16 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
     const uint16_t *ssrc = p.S + (size_t)wg0 * p.N + n0 + Policy::thread_col0(g);
     const size_t wstride = Policy::group_stride(p), cstride = Policy::chunk_stride(p);
     int issued = 0;
+    const bool copyok = Policy::copy_ok(p.N, n0, g);  // this lane's weight chunks exist
     auto issue = [&]() {
-        if (issued < nwg && colok) {
+        if (issued < nwg) {
             const int stage = issued & (kStages - 1);
+            if (copyok) {
 #pragma unroll
-            for (int c = 0; c < Policy::kWords16; ++c)
-                cp_async16(Ring<Policy>::words(ring, stage, c, tid), wsrc + c * cstride);
-            cp_async8(Ring<Policy>::scale(ring, stage, tid), ssrc);
+                for (int c = 0; c < Policy::kWords16; ++c)
+                    cp_async16(Ring<Policy>::words(ring, stage, c, tid), wsrc + c * cstride);
+            }
+            if (colok) cp_async8(Ring<Policy>::scale(ring, stage, tid), ssrc);
         }
         cp_async_commit();
         wsrc += wstride;
@@ -167,10 +213,12 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
     const char *xg = extra + (size_t)(wg0 - cg0) * Policy::kExtraGroupBytes;
     for (int i = 0; i < nwg; ++i) {
         cp_async_wait<kStages - 2>();
+        // a policy that reads other lanes' ring slots needs their copies visible, and
+        // keeps every lane's reads of the previous stage before this iteration's issue
+        if (Policy::kSharedSlots) __syncwarp();
         const int stage = i & (kStages - 1);
-        uint4 w[Policy::kWords16];
-#pragma unroll
-        for (int c = 0; c < Policy::kWords16; ++c) w[c] = *Ring<Policy>::words(ring, stage, c, tid);
+        uint4 w[Policy::kWordRegs];
+        Policy::read_words(ring + stage * Ring<Policy>::kStageBytes, tid, w);
         const uint2 sc = *Ring<Policy>::scale(ring, stage, tid);
         Policy::template compute<DT>(w, sc, arow, rowok, q, xg, acc, g);
         arow += Policy::kActGroupBytes;

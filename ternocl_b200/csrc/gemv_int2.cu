@@ -61,10 +61,19 @@ __device__ __forceinline__ void dec_word(uint32_t x, uint32_t out[8]) {
 
 struct Int2Policy {
     static constexpr int kWords16 = 2;
+    static constexpr int kWordRegs = kWords16;
+    static constexpr bool kSharedSlots = false;
+    __device__ static void read_words(const char *stage, int tid, uint4 *w) {
+#pragma unroll
+        for (int c = 0; c < kWords16; ++c) w[c] = reinterpret_cast<const uint4 *>(stage)[c * gemv::kThreads + tid];
+    }
     static constexpr bool kContiguousCols = true;
     static constexpr int kActGroupBytes = 8 * 32;   // 8 words x 8 slot registers
     static constexpr int kExtraGroupBytes = 0;
+    static constexpr int kActBytesPerK = 2;  // DT activations
+    static constexpr int kActPadBytes = 16;  // row stride = 16 mod 128: 32-byte reads conflict-free
     __device__ static int thread_col0(int g) { return 4 * g; }
+    __device__ static bool copy_ok(int N, int n0, int g) { return n0 + 4 * g < N; }
     __device__ static int thread_col(int g, int i) { return 4 * g + i; }
     // chunk c of group grp: word row kp = 8grp + 4c + q, columns n0+4g .. n0+4g+3
     __device__ static const uint32_t *word_ptr(const gemv::Params &p, int grp, int g, int q, int n0) {
@@ -151,8 +160,7 @@ struct Int2Policy {
 
 template <class DT, int POSTOP, bool OUT_F32>
 cudaError_t launch_t(const GemvArgs &a) {
-    gemv::Params p{(const uint16_t *)a.A, a.B, (const uint16_t *)a.S, nullptr, a.C,
-                   (const uint16_t *)a.Other, a.Bias, a.M, a.N, a.K, a.SK, a.cluster, a.ws_part, a.ws_cnt};
+    gemv::Params p = gemv::gemv_params_impl(a);
     const int G = a.K / kGS;
     const int max_ng = (G + a.SK - 1) / a.SK;
     const int rows = a.M < 8 ? a.M : 8;

@@ -34,6 +34,10 @@ struct GemvArgs {
     float *ws_part = nullptr;    // [SK][M][N] fp32 partials
     unsigned *ws_cnt = nullptr;  // per-tile arrival counters
     cudaStream_t stream = nullptr;
+    // s8 x s2 path
+    const int8_t *Aq = nullptr;
+    const void *SA = nullptr;
+    int qmode = 0;
 };
 
 template <class T>
@@ -97,6 +101,13 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 }
 
 // Kernel-family entry points (one per .cu file).
+cudaError_t quant_a_launch(const void *A, void *SA, int8_t *Aq, int M, int K, int dtype, cudaStream_t s);
+cudaError_t group_dots_launch(const int8_t *Aq, const uint32_t *B, int32_t *D, int M, int N, int K,
+                              cudaStream_t s);
+cudaError_t int8_gemv_launch(const GemvArgs &a);
+cudaError_t int1_gemv_launch(const GemvArgs &a);
+size_t int1_gemv_smem(int M, int K, int SK);
+size_t int8_gemv_smem(int M, int K, int SK);
 cudaError_t int2_gemv_launch(const GemvArgs &a);
 size_t int2_gemv_smem(int M, int K, int SK);
 // tcgen05 / TMEM decode GEMV (gemv_tc.cu): 128 columns and tc_gemv_rows(M) rows per CTA

@@ -9,7 +9,9 @@ from ternocl_b200 import synth
 # with floor = 1e-2 * rms(gold) (near-zero gold values cancel; their absolute error
 # is bounded by the fp32 accumulation error of the much larger partial sums).
 REL_TOL = {0: 2e-3, 1: 1e-2}
-F32_REL_TOL = 2e-5
+# fp32 outputs differ from the gold only by the fp32 reduction order; the reference's
+# own rule for them is rel <= 2e-4 (compare_f32, common/epilogue.hpp:69-77)
+F32_REL_TOL = 2e-4
 
 
 def rel_err(out, gold):

@@ -190,6 +190,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the timed region with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--sets", type=int, default=0,
                     help="weight sets to rotate (default: enough for %.0f GiB)" % WEIGHTS_GIB)
     args = ap.parse_args()
@@ -275,11 +277,15 @@ def main():
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
+        if args.profile_range:
+            torch.cuda.cudart().cudaProfilerStart()
         ev0.record(stream)
         for i in range(args.steps):
             step(i)
         ev1.record(stream)
         barrier()
+        if args.profile_range:
+            torch.cuda.cudart().cudaProfilerStop()
     ms = ev0.elapsed_time(ev1)
     if world > 1:
         t = torch.tensor([ms], device=dev)

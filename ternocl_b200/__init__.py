@@ -160,3 +160,60 @@ def int2_int8_group_dots(Aq, B, stream=None):
     D = torch.empty(M, K // 128, N, dtype=torch.int32, device=Aq.device)
     call("ternocl_int2_int8_group_dots", _ptr(Aq), _ptr(B), _ptr(D), M, N, K, _stream(stream))
     return D
+
+
+def bitcos_upcvt(A, B, S, SR=None, ls=1, postop=0, out_f32=False, other=None, bias=None, out=None,
+                 algo=0, stream=None):
+    """C = epi(A @ decode_bitcos(B) * S); B: one int32 buffer bitmap | offsets | signs | pad,
+    SR: slice_ranks [ls-1, N] (None when ls == 1)."""
+    _check_cuda(A, B, S, SR, other, bias, out)
+    M, K = A.shape
+    N = S.shape[1]
+    C = _out(M, N, A, out_f32, out)
+    call("ternocl_bitcos_upcvt", _ptr(A), _ptr(B), _ptr(S), _ptr(SR), int(ls), _ptr(C), _ptr(other),
+         _ptr(bias), M, N, K, dtype_code(A), int(postop), int(bool(out_f32)), int(algo), _stream(stream))
+    return C
+
+
+def bitcos_random(K, N, z, seed):
+    """Host BITCOS buffer (numpy uint32) of random ternary weights at zero density z."""
+    import numpy as np
+    L = lib()
+    n = L.ternocl_bitcos_random(K, N, float(z), int(seed), None, 0)
+    out = np.empty(n, np.uint32)
+    L.ternocl_bitcos_random(K, N, float(z), int(seed), out.ctypes.data, n)
+    return out
+
+
+def bitcos_pack(codes):
+    """codes [K, N] int8 in {-1, 0, +1} -> host BITCOS buffer (numpy uint32)."""
+    import numpy as np
+    codes = np.ascontiguousarray(codes, np.int8)
+    K, N = codes.shape
+    L = lib()
+    n = L.ternocl_bitcos_pack(codes.ctypes.data, K, N, None, 0)
+    out = np.empty(n, np.uint32)
+    L.ternocl_bitcos_pack(codes.ctypes.data, K, N, out.ctypes.data, n)
+    return out
+
+
+def bitcos_slice_ranks(buf, K, N, ls):
+    """slice_ranks [ls-1, N] (numpy uint32) of a host BITCOS buffer."""
+    import numpy as np
+    buf = np.ascontiguousarray(buf, np.uint32)
+    out = np.zeros((max(ls - 1, 0), N), np.uint32)
+    if ls > 1:
+        call("ternocl_bitcos_slice_ranks", buf.ctypes.data, K, N, ls, out.ctypes.data)
+    return out
+
+
+def hadamard_fwht(x, hb, signs=None, out=None, stream=None):
+    """y = H_hb(signs * x) / sqrt(hb) per hb-wide block of each row of x [rows, K]
+    (fp16/bf16); signs: int8 +-1 [K] or None.  out may be x (in place)."""
+    torch = _torch()
+    _check_cuda(x, signs, out)
+    rows, K = x.shape
+    y = torch.empty_like(x) if out is None else out
+    call("ternocl_hadamard_fwht", _ptr(x), _ptr(signs), _ptr(y), rows, K, int(hb), int(signs is not None),
+         dtype_code(x), _stream(stream))
+    return y

@@ -94,6 +94,12 @@ static GemvPlan gemv_i1_plan(int M, int N, int K, bool allow_ws) {
                        [&](int sk) { return int1_gemv_smem(M, K, sk); });
 }
 
+// BITCOS GEMV (gemv_bitcos.cu): same CTA shape, whole K range staged per CTA
+static GemvPlan gemv_bitcos_plan(int M, int N, int K, bool allow_ws) {
+    return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
+                       [&](int sk) { return bitcos_gemv_smem(M, K, sk); });
+}
+
 // s8 x s2 GEMV (gemv_int8.cu): same CTA shape, int8 activation staging
 static GemvPlan gemv_i8_plan(int M, int N, int K, bool allow_ws) {
     return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
@@ -230,6 +236,40 @@ int ternocl_int1_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
     return cuda_status(int1_gemv_launch(a));
 }
 
+int ternocl_bitcos_upcvt(const void *A, const uint32_t *B, const void *S, const uint32_t *SR, int ls,
+                         void *C, const void *Other, const void *Bias, int M, int N, int K, int dtype,
+                         int postop, int out_f32, int algo, void *stream) {
+    int st = check_gemm_common(A, B, S, C, Other, Bias, M, N, K, dtype, postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (ls < 1) return TERNOCL_ERR_ARG;
+    if (K % (64 * ls)) return TERNOCL_ERR_SHAPE;  // bitcos_fp16_upcvt/main.cpp:129
+    if (ls > 1 && !SR) return TERNOCL_ERR_ARG;
+    if (algo < TERNOCL_ALGO_AUTO || algo > TERNOCL_ALGO_GEMM) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    GemvArgs a;
+    a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
+    a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.SR = SR; a.ls = ls;
+    a.stream = (cudaStream_t)stream;
+    // no workspace in this signature: split-K stays within one thread-block cluster
+    const GemvPlan p = gemv_bitcos_plan(M, N, K, false);
+    if (bitcos_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    a.SK = p.SK;
+    a.cluster = p.cluster ? 1 : 0;
+    return cuda_status(bitcos_gemv_launch(a));
+}
+
+int ternocl_hadamard_fwht(const void *x, const int8_t *signs, void *y, int rows, int K, int hb, int use_signs,
+                          int dtype, void *stream) {
+    if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
+    if (hb < 256 || hb > 4096 || (hb & (hb - 1))) return TERNOCL_ERR_SHAPE;  // hadamard_fwht.cl:17-31
+    if (rows < 0 || K <= 0 || K % hb) return TERNOCL_ERR_SHAPE;                // bpr = K / HB (:68)
+    if (!x || !y || (use_signs && !signs)) return TERNOCL_ERR_ARG;
+    if (!aligned(x, 16) || !aligned(y, 16) || (use_signs && !aligned(signs, 16))) return TERNOCL_ERR_ARG;
+    if (rows == 0) return TERNOCL_OK;
+    return cuda_status(hadamard_launch(x, signs, y, rows, K, hb, use_signs ? 1 : 0, dtype, (cudaStream_t)stream));
+}
+
 int ternocl_int8_ldsa(int M) { return (M + 31) & ~31; }
 
 int ternocl_int8_quant_a(const void *A, void *SA, int8_t *Aq, int M, int K, int dtype, void *stream) {
@@ -273,13 +313,6 @@ int ternocl_int2_int8_group_dots(const int8_t *Aq, const uint32_t *B, int32_t *D
 }
 
 // ---- entry points whose kernels are not built yet: report UNSUPPORTED ----------
-int ternocl_bitcos_upcvt(const void *, const uint32_t *, const void *, const uint32_t *, int, void *,
-                         const void *, const void *, int, int, int, int, int, int, int, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
-}
-int ternocl_hadamard_fwht(const void *, const int8_t *, void *, int, int, int, int, int, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
-}
 int ternocl_moe_rows_per_tile(void) { return 128; }
 int ternocl_moe_route(const int32_t *, int32_t *, int32_t *, int32_t *, int, int, int, void *) {
     return TERNOCL_ERR_UNSUPPORTED;

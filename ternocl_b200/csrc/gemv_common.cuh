@@ -38,7 +38,8 @@ struct Params {
     const uint16_t *A;
     const uint32_t *B;
     const uint16_t *S;
-    const uint32_t *SR;  // BITCOS slice ranks (unused by the other layouts)
+    const uint32_t *SR;  // BITCOS slice ranks [ls-1][N] (unused by the other layouts)
+    int ls;
     void *C;
     const uint16_t *Other;
     const void *Bias;
@@ -84,7 +85,8 @@ inline Params gemv_params_impl(const GemvArgs &a) {
     p.A = (const uint16_t *)a.A;
     p.B = a.B;
     p.S = (const uint16_t *)a.S;
-    p.SR = nullptr;
+    p.SR = a.SR;
+    p.ls = a.ls;
     p.C = a.C;
     p.Other = (const uint16_t *)a.Other;
     p.Bias = a.Bias;
@@ -148,6 +150,116 @@ __host__ __device__ inline size_t smem_bytes(int rows, int krange) {
     const size_t red = (size_t)kWarps * 32 * 8 * sizeof(float);  // warp partials + CTA partial
     const size_t ring = Ring<Policy>::kBytes;
     return (ring > red ? ring : red) + act + Policy::extra_smem(rows, krange);
+}
+
+// Reduction over the CTA's K-split warps (in warp order, through `smem`, >= 8 KB),
+// then over the SK CTAs of the strip (cluster DSMEM or workspace, in split order),
+// and the epilogue store.  v[h*4 + i] = this thread's partial for activation row
+// mb+2q+h and column n0 + ColMap::thread_col(g, i).  Callers synchronise the CTA
+// before reusing `smem`.
+template <class ColMap, class DT, int POSTOP, bool OUT_F32>
+__device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], bool colok) {
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, q = lane & 3;
+    const int n0 = blockIdx.x * 32;
+    const int mb = blockIdx.z * 8;
+    const int sk = blockIdx.y;
+    float(*red)[32][8] = reinterpret_cast<float(*)[32][8]>(smem);  // [kWarps][lane][8]
+    if (warp > 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) red[warp - 1][lane][i] = v[i];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int w = 0; w < kWarps - 1; ++w)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] += red[w][lane][i];
+    }
+
+    int cols[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) cols[i] = n0 + ColMap::thread_col(g, i);
+
+    auto store = [&]() {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = mb + 2 * q + h;
+            if (m < p.M) {
+                if (ColMap::kContiguousCols) {
+                    epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[0], v[4 * h], v[4 * h + 1]);
+                    epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[2], v[4 * h + 2], v[4 * h + 3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        epi_store<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[i], v[4 * h + i]);
+                }
+            }
+        }
+    };
+
+    if (p.SK == 1) {
+        if (warp == 0 && colok) store();
+        return;
+    }
+    if (p.cluster) {
+        // split-K across the CTAs of a cluster: partials through distributed shared
+        // memory, summed by cluster rank 0 in rank (= K split) order
+        float *mine = &red[kWarps - 1][lane][0];
+        if (warp == 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mine[i] = v[i];
+        }
+        cluster_sync_all();
+        if (cluster_ctarank() == 0 && warp == 0) {
+            const uint32_t la = smem_u32(mine);
+            for (int r = 1; r < p.SK; ++r) {
+                const float4 x0 = ld_dsmem_f4(la, (uint32_t)r);
+                const float4 x1 = ld_dsmem_f4(la + 16, (uint32_t)r);
+                v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+                v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+            }
+            if (colok) store();
+        }
+        cluster_sync_all();  // keep every CTA's partial alive until rank 0 has read it
+        return;
+    }
+    if (warp != 0) return;
+    if (colok) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = mb + 2 * q + h;
+            if (m < p.M) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) __stcg(p.ws_part + ((size_t)sk * p.M + m) * p.N + cols[i], v[4 * h + i]);
+            }
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    const unsigned tile = blockIdx.z * gridDim.x + blockIdx.x;
+    unsigned last = 0;
+    if (lane == 0) last = (atomicAdd(&p.ws_cnt[tile], 1u) == (unsigned)(p.SK - 1)) ? 1u : 0u;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    if (colok) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = mb + 2 * q + h;
+            if (m < p.M) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float t = 0.0f;
+                    for (int s = 0; s < p.SK; ++s) t += __ldcg(p.ws_part + ((size_t)s * p.M + m) * p.N + cols[i]);
+                    v[4 * h + i] = t;
+                }
+            }
+        }
+        store();
+    }
+    if (lane == 0) p.ws_cnt[tile] = 0u;  // ready for the next call
 }
 
 template <class Policy, class DT, int POSTOP, bool OUT_F32>
@@ -228,105 +340,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
     cp_async_wait<0>();
     pdl_launch_dependents();
 
-    // in-CTA reduction over the K-split warps, in warp order (ring memory reused)
     float v[8];
     Policy::thread_values(acc, v);  // v[h*4 + i]: activation row mb+2q+h, column col(i)
-    __syncthreads();
-    float(*red)[32][8] = reinterpret_cast<float(*)[32][8]>(smem);  // [kWarps][lane][8]
-    if (warp > 0) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) red[warp - 1][lane][i] = v[i];
-    }
-    __syncthreads();
-    if (warp == 0) {
-#pragma unroll
-        for (int w = 0; w < kWarps - 1; ++w)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] += red[w][lane][i];
-    }
-
-    int cols[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) cols[i] = n0 + Policy::thread_col(g, i);
-
-    auto store = [&]() {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int m = mb + 2 * q + h;
-            if (m < p.M) {
-                if (Policy::kContiguousCols) {
-                    epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[0], v[4 * h], v[4 * h + 1]);
-                    epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[2], v[4 * h + 2], v[4 * h + 3]);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        epi_store<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, cols[i], v[4 * h + i]);
-                }
-            }
-        }
-    };
-
-    if (p.SK == 1) {
-        if (warp == 0 && colok) store();
-        return;
-    }
-    if (p.cluster) {
-        // split-K across the CTAs of a cluster: partials through distributed shared
-        // memory, summed by cluster rank 0 in rank (= K split) order
-        float *mine = &red[kWarps - 1][lane][0];
-        if (warp == 0) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) mine[i] = v[i];
-        }
-        cluster_sync_all();
-        if (cluster_ctarank() == 0 && warp == 0) {
-            const uint32_t la = smem_u32(mine);
-            for (int r = 1; r < p.SK; ++r) {
-                const float4 x0 = ld_dsmem_f4(la, (uint32_t)r);
-                const float4 x1 = ld_dsmem_f4(la + 16, (uint32_t)r);
-                v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
-                v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
-            }
-            if (colok) store();
-        }
-        cluster_sync_all();  // keep every CTA's partial alive until rank 0 has read it
-        return;
-    }
-    if (warp != 0) return;
-    if (colok) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int m = mb + 2 * q + h;
-            if (m < p.M) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) __stcg(p.ws_part + ((size_t)sk * p.M + m) * p.N + cols[i], v[4 * h + i]);
-            }
-        }
-    }
-    __threadfence();
-    __syncwarp();
-    const unsigned tile = blockIdx.z * gridDim.x + blockIdx.x;
-    unsigned last = 0;
-    if (lane == 0) last = (atomicAdd(&p.ws_cnt[tile], 1u) == (unsigned)(p.SK - 1)) ? 1u : 0u;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    if (colok) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int m = mb + 2 * q + h;
-            if (m < p.M) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float t = 0.0f;
-                    for (int s = 0; s < p.SK; ++s) t += __ldcg(p.ws_part + ((size_t)s * p.M + m) * p.N + cols[i]);
-                    v[4 * h + i] = t;
-                }
-            }
-        }
-        store();
-    }
-    if (lane == 0) p.ws_cnt[tile] = 0u;  // ready for the next call
+    __syncthreads();  // the ring is reused for the reduction
+    finish<Policy, DT, POSTOP, OUT_F32>(p, smem, v, colok);
 }
 
 }  // namespace gemv

@@ -38,6 +38,9 @@ struct GemvArgs {
     const int8_t *Aq = nullptr;
     const void *SA = nullptr;
     int qmode = 0;
+    // BITCOS: slice ranks [ls-1][N] of the reference's ls K slices
+    const uint32_t *SR = nullptr;
+    int ls = 1;
 };
 
 template <class T>
@@ -106,6 +109,10 @@ cudaError_t group_dots_launch(const int8_t *Aq, const uint32_t *B, int32_t *D, i
                               cudaStream_t s);
 cudaError_t int8_gemv_launch(const GemvArgs &a);
 cudaError_t int1_gemv_launch(const GemvArgs &a);
+cudaError_t bitcos_gemv_launch(const GemvArgs &a);
+cudaError_t hadamard_launch(const void *x, const int8_t *signs, void *y, int rows, int K, int hb, int use_signs,
+                            int dtype, cudaStream_t st);
+size_t bitcos_gemv_smem(int M, int K, int SK);
 size_t int1_gemv_smem(int M, int K, int SK);
 size_t int8_gemv_smem(int M, int K, int SK);
 cudaError_t int2_gemv_launch(const GemvArgs &a);

@@ -82,3 +82,18 @@ def test_gemv_deterministic(cuda, tl):
     ws = tl.Workspace()
     outs = [run(tl, c, 1, 0, False, w) for w in (None, ws, None, ws)]
     assert np.array_equal(outs[0], outs[2]) and np.array_equal(outs[1], outs[3])
+
+
+def test_decode_bit_exact(cuda, tl):
+    # A = identity: C[k, n] = sgn(k, n) * S exactly, i.e. the decoded weights of the
+    # sel layout, compared with the per-column bit order the gold reads (main.cpp:76)
+    K, N = 512, 96
+    rng = np.random.default_rng(8)
+    Bpc = rng.integers(0, 1 << 32, size=(K // 32, N), dtype=np.uint64).astype(np.uint32)
+    c = dict(A=synth.to_dt(np.eye(K), 0), sel=orc.int1_to_sel(Bpc, K, N), S=synth.to_dt(np.ones((K // 128, N)), 0),
+             other=None, bias=None)
+    out = synth.from_dt(run(tl, c, 0, 0, False), 0)
+    k = np.arange(K)
+    pos = np.array([synth.int1_bit_pos(x) for x in k], np.uint32)[:, None]
+    neg = (Bpc[k // 32][:, :] >> pos) & 1
+    assert np.array_equal(out, np.where(neg == 1, -1.0, 1.0).astype(np.float32))

@@ -84,3 +84,19 @@ def test_gemv_ragged_rows_untouched(cuda, tl):
     big = torch.full((M + 2, N), 7.0, dtype=torch.float16, device="cuda")
     tl.int2_upcvt(A, B, S, out=big[:M], algo=tl.ALGO_GEMV)
     assert torch.all(big[M:] == 7.0)
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+def test_decode_bit_exact(cuda, tl, algo):
+    # A = identity: C[k, n] = value(code(k, n)) * S exactly (one non-zero term), i.e.
+    # the decoded weights; every 2-bit code, as code_to_value reads it (main.cpp:76)
+    from ternocl_b200 import synth
+    K, N = 512, 96
+    rng = np.random.default_rng(8)
+    B = rng.integers(0, 1 << 32, size=(K // 16, N), dtype=np.uint64).astype(np.uint32)
+    S = synth.to_dt(np.ones((K // 128, N)), 0)
+    c = dict(A=synth.to_dt(np.eye(K), 0), B=B, S=S, other=None, bias=None)
+    out = synth.from_dt(run(tl, c, K, K, N, 0, 0, False, algo, tl.Workspace()), 0)
+    k = np.arange(K)[:, None]
+    codes = (B[k // 16, np.arange(N)[None, :]] >> (2 * (k % 16)).astype(np.uint32)) & 3
+    assert np.array_equal(out, np.array([0, 1, -2, -1], np.float32)[codes])

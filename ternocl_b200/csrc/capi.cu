@@ -181,6 +181,8 @@ int ternocl_device_error(int reset) {
     unsigned v = 0, t = 0;
     if (read_device_error_gemv_tc(&t, reset) != cudaSuccess) return -1;
     v |= t;
+    if (read_device_error_gemm_tc(&t, reset) != cudaSuccess) return -1;
+    v |= t;
     return (int)v;
 }
 
@@ -195,7 +197,8 @@ int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
     a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.stream = (cudaStream_t)stream;
-    // (the tensor-core GEMM path is selected for large M once available)
+    if (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM))
+        return cuda_status(int2_gemm_tc_launch(a));
     const bool simt = algo != TERNOCL_ALGO_GEMV_TMEM;
     GemvPlan p = simt ? gemv_plan(M, N, K, ws != nullptr) : gemv_tc_plan(M, N, K, ws != nullptr);
     if (p.total() > ws_bytes) p = simt ? gemv_plan(M, N, K, false) : gemv_tc_plan(M, N, K, false);
@@ -223,6 +226,8 @@ int ternocl_int1_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
     a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.stream = (cudaStream_t)stream;
+    if (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM))
+        return cuda_status(int1_gemm_tc_launch(a));
     GemvPlan p = gemv_i1_plan(M, N, K, ws != nullptr);
     if (p.total() > ws_bytes) p = gemv_i1_plan(M, N, K, false);
     if (int1_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;

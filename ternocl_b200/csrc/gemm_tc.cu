@@ -1,0 +1,359 @@
+// Prefill GEMM on the 5th-generation tensor cores (tcgen05), replaces the M-tiled
+// upconvert kernels int2_fp16_upcvt_gemm_mt (int2_fp16_upcvt.cl:338-396) and
+// int1_fp16_upcvt_gemm_mt (int1_fp16_upcvt.cl:302-352):
+//
+//   C[m,n] = DT(epi( sum_k A[m,k] * W[k,n] )),   W[k,n] = code(k,n) * S[k/128, n]
+//
+// As in the reference's GEMM the weights are upconverted to DT +-s (or 0) before the
+// MMA (exact: s is a DT value), and the products are accumulated in fp32.
+//
+// CTA tile 128 (M) x 256 (N), K in steps of 64; 320 threads in three roles:
+//   warp 0      TMA producer: A [128 x 64] through a 2-D tensor map (8 boxes of 128
+//               rows x 16 bytes = the no-swizzle K-major core-matrix layout), the
+//               packed weight rows and the scale row through 1-D bulk copies, all
+//               completing on one mbarrier per stage (4 load stages);
+//   warp 1      TMEM allocation (256 fp32 columns) and the MMA issuer: per stage four
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16), A and B from
+//               shared-memory descriptors, accumulator in TMEM; tcgen05.commit frees
+//               the stage and the decoded buffer;
+//   warps 2-9   decode: warp kc, lane nb turns the packed words of 8 columns
+//               (8nb..8nb+7) and 8 K rows (8kc..8kc+7 of the stage) into one 8x8
+//               core matrix of the B operand, MN-major (a core-matrix row = one K row,
+//               8 consecutive columns, 16 bytes), 3 decode buffers; after the K loop
+//               the same warps read the accumulator (tcgen05.ld, warp w owns TMEM lanes
+//               32(w%4)..+31) and run the fused epilogue store.
+// Every mbarrier wait is bounded (tc::mbar_wait); on a timeout the roles skip ahead,
+// the producer waits (bounded) for its copies in flight, and TMEM is freed.
+//
+// The decode of a layout is a policy:
+//   Int2Gemm  word (kp,n) = 16 rows; columns n, n+1 of the same 8 rows are paired with
+//             one PRMT, decoded as a half2 (row r of column n, row r of column n+1) by
+//             the same LOP3 + HSUB2 as the GEMV (Int2Decode), then scaled by HMUL2;
+//   Int1Gemm  sel layout: word (kp, blk+p) = rows (2p, 2p+1) of 16 columns; one IMAD
+//             puts the sign bits of columns (2i, 2i+1) of a row at bits 15 and 31 and
+//             one LOP3 applies them to the scale pair: +-s exactly.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "launch.h"
+#include "tc_common.cuh"
+
+namespace ternocl {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int kLoadStages = 4, kDecStages = 3;
+constexpr int kDecWarps = 8;
+constexpr int kThreads = (2 + kDecWarps) * 32;
+// decoded B (MN-major, no swizzle): core matrix (kc, nb) at nb * kDecSBO + kc * 128;
+// the 16-byte pad in kDecSBO spreads the decode warps' stores over all banks
+constexpr int kDecLBO = 128, kDecSBO = BK / 8 * 128 + 16;  // 1040
+constexpr int kDecStageBytes = (BN / 8) * kDecSBO;         // 33280
+// A (K-major, no swizzle): box c (K = 8c .. 8c+7) = 128 rows x 16 bytes at c * 2048
+constexpr int kALBO = BM * 16, kASBO = 128;
+constexpr int kAStageBytes = BM * BK * 2;  // 16384
+constexpr int kPackStageBytes = 4096;      // int2: 4 word rows x 256 columns; int1: 2 x 256
+constexpr int kScaleStageBytes = BN * 2;
+constexpr int kTmemCols = BN;
+
+struct Smem {
+    // decoded buffers first: every descriptor-derived address stays inside the block
+    static constexpr int dec = 0;
+    static constexpr int a = dec + kDecStages * kDecStageBytes;  // 99840 (1024-aligned below)
+    static constexpr int a_al = (a + 1023) / 1024 * 1024;
+    static constexpr int pack = a_al + kLoadStages * kAStageBytes;
+    static constexpr int scale = pack + kLoadStages * kPackStageBytes;
+    static constexpr int bars = scale + kLoadStages * kScaleStageBytes;
+    static constexpr int total = bars + 256;
+};
+
+struct Params {
+    const uint32_t *B;
+    const uint16_t *S;
+    void *C;
+    const uint16_t *Other;
+    const void *Bias;
+    int M, N, K;
+};
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            tc::smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(tc::smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_ss_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+template <class DT>
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (DT::kBF16) asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+    else asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// ---- int2: [K/16, N] words, 4 word rows per stage --------------------------------
+struct Int2Gemm {
+    static constexpr int kRowsPerStage = BK / 16;  // packed word rows per stage
+    __device__ static const uint32_t *row_ptr(const Params &p, int kb, int r, int n0) {
+        return p.B + (size_t)(kb * kRowsPerStage + r) * p.N + n0;
+    }
+    // core matrix rows out[r] (K row 8kc + r; columns 8nb .. 8nb+7 as 4 half2)
+    template <class DT>
+    __device__ static void decode(const char *pack, const uint16_t *scale, int kc, int nb, uint4 out[8]) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(pack + (kc >> 1) * (BN * 4) + nb * 32);
+        const uint4 w0 = src[0], w1 = src[1];
+        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint4 sv = *reinterpret_cast<const uint4 *>(scale + nb * 8);
+        const uint32_t s2[4] = {sv.x, sv.y, sv.z, sv.w};  // (s_{2i}, s_{2i+1})
+        const uint32_t sel = (kc & 1) ? 0x7632u : 0x5410u;  // rows 8..15 or 0..7 of the words
+        uint32_t d[4][8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t z = __byte_perm(w[2 * i], w[2 * i + 1], sel);  // (column 2i | column 2i+1)
+            Int2Decode<DT>::word(z, d[i]);                                   // d[i][r] = (row r of both)
+#pragma unroll
+            for (int r = 0; r < 8; ++r) d[i][r] = hmul2<DT>(d[i][r], s2[i]);
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) out[r] = make_uint4(d[0][r], d[1][r], d[2][r], d[3][r]);
+    }
+};
+
+// ---- int1: sel layout [K/32, N], 2 word rows per stage --------------------------
+struct Int1Gemm {
+    static constexpr int kRowsPerStage = BK / 32;
+    __device__ static const uint32_t *row_ptr(const Params &p, int kb, int r, int n0) {
+        return p.B + (size_t)(kb * kRowsPerStage + r) * p.N + n0;
+    }
+    template <class DT>
+    __device__ static void decode(const char *pack, const uint16_t *scale, int kc, int nb, uint4 out[8]) {
+        // K rows 8kc..8kc+7 of the stage = K32 row kc/4, row pairs p = 4(kc%4) .. +3;
+        // columns 8nb..8nb+7 = half (nb & 1) of the words of 16-column block nb/2
+        const uint4 wv = *reinterpret_cast<const uint4 *>(pack + (kc >> 2) * (BN * 4) + (nb >> 1) * 64 +
+                                                          (kc & 3) * 16);
+        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint4 sv = *reinterpret_cast<const uint4 *>(scale + nb * 8);
+        const uint32_t s2[4] = {sv.x, sv.y, sv.z, sv.w};
+        const int sh = 16 * (nb & 1);
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+            const uint32_t h = w[pp] >> sh;  // bit 2c + r: column 8nb + c, row 2p + r
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                uint32_t o[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    // bits 4i + r (column 2i) -> 15, 4i + 2 + r (column 2i+1) -> 31
+                    const uint32_t t = (h >> (4 * i + r)) & 5u;
+                    uint32_t v;
+                    asm("lop3.b32 %0, %1, %2, %3, 0x6A;\n" : "=r"(v) : "r"(t * 0x20008000u), "n"(0x80008000u), "r"(s2[i]));
+                    o[i] = v;  // (t*K & 0x80008000) ^ s2: the sign bits applied to (s_2i, s_2i+1)
+                }
+                out[2 * pp + r] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
+    }
+};
+
+template <class Policy, class DT, int POSTOP, bool OUT_F32>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tmA) {
+    extern __shared__ __align__(1024) char smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int nk = p.K / BK;
+    const int ncols = min(BN, p.N - n0);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars);
+    uint64_t *load_empty = full + kLoadStages;
+    uint64_t *dec_full = load_empty + kLoadStages;
+    uint64_t *dec_empty = dec_full + kDecStages;
+    uint64_t *acc_full = dec_empty + kDecStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+
+    if (tid == 0) {
+        for (int s = 0; s < kLoadStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&load_empty[s], 1 + kDecWarps);
+        }
+        for (int d = 0; d < kDecStages; ++d) {
+            tc::mbar_init(&dec_full[d], kDecWarps);
+            tc::mbar_init(&dec_empty[d], 1);
+        }
+        tc::mbar_init(acc_full, 1);
+        tc::fence_mbar_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            pdl_wait();
+            const uint32_t pack_bytes = Policy::kRowsPerStage * ncols * 4, scale_bytes = ncols * 2;
+            int issued = 0;
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % kLoadStages;
+                if (kb >= kLoadStages && !tc::mbar_wait(&load_empty[s], ((kb / kLoadStages) - 1) & 1)) break;
+                tc::mbar_expect_tx(&full[s], kAStageBytes + pack_bytes + scale_bytes);
+                char *a = smem + Smem::a_al + s * kAStageBytes;
+#pragma unroll
+                for (int c = 0; c < BK / 8; ++c) tma_load_2d(a + c * kALBO, &tmA, kb * BK + 8 * c, m0, &full[s]);
+                char *pk = smem + Smem::pack + s * kPackStageBytes;
+                for (int r = 0; r < Policy::kRowsPerStage; ++r)
+                    tc::bulk_g2s(pk + r * (BN * 4), Policy::row_ptr(p, kb, r, n0), pack_bytes / Policy::kRowsPerStage,
+                                 &full[s]);
+                tc::bulk_g2s(smem + Smem::scale + s * kScaleStageBytes, p.S + (size_t)(kb * BK / kGS) * p.N + n0,
+                             scale_bytes, &full[s]);
+                ++issued;
+            }
+            // copies still in flight must land before the block can exit
+            for (int kb = issued - kLoadStages < 0 ? 0 : issued - kLoadStages; kb < issued; ++kb)
+                tc::mbar_wait(&full[kb % kLoadStages], (kb / kLoadStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_f16(DT::kBF16, BM, BN) | (1u << 16);  // B MN-major
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % kLoadStages, d = kb % kDecStages;
+                if (!tc::mbar_wait(&full[s], (kb / kLoadStages) & 1)) break;
+                if (!tc::mbar_wait(&dec_full[d], (kb / kDecStages) & 1)) break;
+                tc::fence_after_sync();
+                const uint32_t a = tc::smem_addr(smem + Smem::a_al + s * kAStageBytes);
+                const uint32_t b = tc::smem_addr(smem + Smem::dec + d * kDecStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t ad = tc::sdesc_kmajor_noswz(a + kk * 2 * kALBO, kALBO, kASBO);
+                    const uint64_t bd = tc::sdesc_kmajor_noswz(b + kk * 2 * kDecLBO, kDecLBO, kDecSBO);
+                    mma_ss_f16(tmem, ad, bd, idesc, (kb | kk) != 0);
+                }
+                tc::mma_commit(&load_empty[s]);
+                tc::mma_commit(&dec_empty[d]);
+            }
+            tc::mma_commit(acc_full);
+        }
+    } else {
+        // ---------------- decode, then epilogue ----------------
+        const int kc = warp - 2, nb = lane;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % kLoadStages, d = kb % kDecStages;
+            if (!tc::mbar_wait(&full[s], (kb / kLoadStages) & 1)) break;
+            if (kb >= kDecStages && !tc::mbar_wait(&dec_empty[d], ((kb / kDecStages) - 1) & 1)) break;
+            uint4 rows[8];
+            Policy::template decode<DT>(smem + Smem::pack + s * kPackStageBytes,
+                                        reinterpret_cast<const uint16_t *>(smem + Smem::scale + s * kScaleStageBytes),
+                                        kc, nb, rows);
+            char *dst = smem + Smem::dec + d * kDecStageBytes + nb * kDecSBO + kc * 128;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4 *>(dst + r * 16) = rows[r];
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tc::mbar_arrive(&dec_full[d]);
+                tc::mbar_arrive(&load_empty[s]);
+            }
+        }
+        if (tc::mbar_wait(acc_full, 0)) {
+            tc::fence_after_sync();
+            const int quad = warp & 3, half = kc >> 2;
+            const int m = m0 + 32 * quad + lane;
+#pragma unroll 1
+            for (int c = 0; c < BN / 2 / 16; ++c) {
+                const int col = half * (BN / 2) + 16 * c;
+                float v[16];
+                tc::tmem_ld<16>(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)col, v);
+                tc::tmem_wait_ld();
+                if (m < p.M && col < ncols) {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2)
+                        epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, n0 + col + i, v[i], v[i + 1]);
+                }
+            }
+        }
+        pdl_launch_dependents();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)f;
+    }
+    return fn;
+}
+
+// A [M, K] DT row-major; boxes of 128 rows x 8 elements, rows past M read as zero
+static cudaError_t make_map_a(CUtensorMap *map, const void *A, int M, int K, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {8, BM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                          const_cast<void *>(A), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <class Policy>
+cudaError_t launch_policy(const GemvArgs &a) {
+    CUtensorMap map;
+    cudaError_t e = make_map_a(&map, a.A, a.M, a.K, a.dtype == TERNOCL_BF16);
+    if (e != cudaSuccess) return e;
+    Params p;
+    p.B = a.B;
+    p.S = (const uint16_t *)a.S;
+    p.C = a.C;
+    p.Other = (const uint16_t *)a.Other;
+    p.Bias = a.Bias;
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
+        using DT = typename decltype(dt)::type;
+        auto kern = gemm_kernel<Policy, DT, decltype(po)::value, decltype(of)::value>;
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total);
+        if (err != cudaSuccess) return err;
+        const dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
+        return launch_kernel(kern, grid, dim3(kThreads), (size_t)Smem::total, a.stream, p, map);
+    });
+}
+
+}  // namespace gemm
+
+cudaError_t int2_gemm_tc_launch(const GemvArgs &a) { return gemm::launch_policy<gemm::Int2Gemm>(a); }
+cudaError_t int1_gemm_tc_launch(const GemvArgs &a) { return gemm::launch_policy<gemm::Int1Gemm>(a); }
+cudaError_t read_device_error_gemm_tc(unsigned *out, int reset) { return tc::read_tu_error(out, reset); }
+
+}  // namespace ternocl

@@ -45,6 +45,10 @@ constexpr int kThreads = gemv::kThreads;
 constexpr int kMetaBytes = 2048;  // ranks and per-column sign-window bookkeeping
 constexpr int kRedBytes = gemv::kWarps * 32 * 8 * 4;  // gemv::finish's reduction area (>= the 2 KB table)
 
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(gemv::smem_u32(dst)), "l"(src));
+}
+
 struct BitcosCols {
     static constexpr bool kContiguousCols = true;
     __device__ static int thread_col(int g, int i) { return 4 * g + i; }
@@ -104,40 +108,46 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
         lut[idx] = make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
     }
 
-    // 1. bitmap words and scales of the range (weights: staged before the PDL wait)
+    // 1. bitmap words and scales of the range (weights: staged before the PDL wait),
+    //    16-byte cp.async chunks: a bitmap row of 32 columns is 8 chunks, a scale row 4
     const uint32_t *B = p.B;
     const int nkp = 4 * ng;
-    for (int idx = tid; idx < nkp * 32; idx += kThreads) {
-        const int kp = idx >> 5, c = idx & 31;
-        sbm[idx] = (n0 + c < N) ? __ldg(B + (size_t)(cg0 * 4 + kp) * N + n0 + c) : 0u;
+    const int ncol = min(32, N - n0);  // 16 or 32 (N % 16 == 0)
+    for (int idx = tid; idx < nkp * 8; idx += kThreads) {
+        const int kp = idx >> 3, ch = idx & 7;
+        if (ch * 4 < ncol) gemv::cp_async16(sbm + kp * 32 + ch * 4, B + (size_t)(cg0 * 4 + kp) * N + n0 + ch * 4);
     }
-    for (int idx = tid; idx < ng * 32; idx += kThreads) {
-        const int gi = idx >> 5, c = idx & 31;
-        ssc[idx] = (n0 + c < N) ? __ldg(p.S + (size_t)(cg0 + gi) * N + n0 + c) : (uint16_t)0;
+    for (int idx = tid; idx < ng * 4; idx += kThreads) {
+        const int gi = idx >> 2, ch = idx & 3;
+        if (ch * 8 < ncol) gemv::cp_async16(ssc + gi * 32 + ch * 8, p.S + (size_t)(cg0 + gi) * N + n0 + ch * 8);
     }
+    gemv::cp_async_commit();
     // 2. popcount between the enclosing reference slice's boundary and the range start
     const int slice_rows = K / p.ls;
     const int s0 = (cg0 * kGS) / slice_rows;
     {
         const int kp_from = s0 * slice_rows / 32, kp_to = cg0 * 4;
         uint32_t cnt = 0;
-        if (n0 + lane < N)
+        if (lane < ncol) {
+#pragma unroll 8
             for (int kp = kp_from + warp; kp < kp_to; kp += gemv::kWarps)
                 cnt += __popc(__ldg(B + (size_t)kp * N + n0 + lane));
+        }
         pre[warp * 32 + lane] = cnt;
     }
+    gemv::cp_async_wait<0>();
     __syncthreads();
-    // 3. popcount of each warp's sub-range
+    // 3. popcount of each warp's sub-range (columns >= N hold stale words: not used)
     {
         uint32_t cnt = 0;
         for (int kp = (wg0 - cg0) * 4; kp < (wg1 - cg0) * 4; ++kp) cnt += __popc(sbm[kp * 32 + lane]);
-        seg[warp * 32 + lane] = cnt;
+        seg[warp * 32 + lane] = lane < ncol ? cnt : 0u;
     }
     __syncthreads();
     const size_t bw = (size_t)(K / 32) * N;
     if (tid < 32) {
         const int c = tid;
-        const bool ok = n0 + c < N;
+        const bool ok = c < ncol;
         uint32_t r = (ok && s0 > 0) ? __ldg(p.SR + (size_t)(s0 - 1) * N + n0 + c) : 0u;
         r += pre[c] + pre[32 + c] + pre[64 + c] + pre[96 + c];
 #pragma unroll
@@ -152,22 +162,23 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
         scnt[c] = ok ? (r >> 5) + 2 - wlo : 0u;  // windows read words rank/32 and rank/32 + 1
     }
     __syncthreads();
-    // 4. the sign words of each column's range (contiguous in the stream)
+    // 4. the sign words of each column's range (contiguous in the stream, 4-byte copies)
     const uint32_t *signs = B + bw + N;
-    for (int c = warp; c < 32; c += gemv::kWarps) {
-        const uint32_t cnt = scnt[c];
-        const uint32_t *src = signs + soff[c] + swlo[c];
-        for (uint32_t i = lane; i < cnt; i += 32) ssg[c * cap + i] = __ldg(src + i);
+    for (int idx = tid; idx < 32 * cap; idx += kThreads) {
+        const int c = idx / cap, i = idx - c * cap;
+        if ((uint32_t)i < scnt[c]) cp_async4(ssg + idx, signs + soff[c] + swlo[c] + i);
     }
     // 5. activations, 16-byte unit u stored at u ^ (((u >> 3) & 1) << 1)
     pdl_wait();
     const int nu = krange / 8;
     for (int it = tid; it < rows * nu; it += kThreads) {
         const int m = it / nu, u = it - m * nu;
-        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p.A + (size_t)(mb + m) * K + (size_t)cg0 * kGS) + u);
         const int pu = u ^ (((u >> 3) & 1) << 1);
-        *reinterpret_cast<uint4 *>(act + (size_t)m * act_stride + (size_t)pu * 16) = v;
+        gemv::cp_async16(act + (size_t)m * act_stride + (size_t)pu * 16,
+                         p.A + (size_t)(mb + m) * K + (size_t)cg0 * kGS + (size_t)u * 8);
     }
+    gemv::cp_async_commit();
+    gemv::cp_async_wait<0>();
     __syncthreads();
 
     float acc[2][4];

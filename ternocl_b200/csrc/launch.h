@@ -122,6 +122,12 @@ int tc_gemv_rows(int M);
 size_t int2_gemv_tc_smem(int M, int K, int SK);
 cudaError_t int2_gemv_tc_launch(const GemvArgs &a);
 cudaError_t read_device_error_gemv_tc(unsigned *out, int reset);
+// tcgen05 prefill GEMM (gemm_tc.cu): 128 x 256 tiles, weights upconverted in shared memory
+cudaError_t int2_gemm_tc_launch(const GemvArgs &a);
+cudaError_t int1_gemm_tc_launch(const GemvArgs &a);
+cudaError_t read_device_error_gemm_tc(unsigned *out, int reset);
+// M from which TERNOCL_ALGO_AUTO picks the GEMM (int2_fp16_upcvt/main.cpp:160)
+constexpr int kGemmMinM = 64;
 // split-K factor the register-decode GEMV's planner picks when a workspace exists
 int gemv_split_k(int M, int N, int K);
 // CUDA error -> ternocl status (records ternocl_last_error)

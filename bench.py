@@ -16,6 +16,10 @@ from the 126 MB L2).  One step = one GEMV per shape, each on the next weight set
   cpu_baseline  the reference's own host gold (compute_gold, compiled from the
              reference sources into oracle/_ref) on the host cores, bounded sample
 
+Secondary figure on the same line (`secondary.prefill`, 1 GPU): the M=2048 int2 fp16
+prefill GEMM (tcgen05) on the same four shapes, TFLOP/s (2*M*N*K per GEMM) against the
+measured sustained bf16 GEMM peak.  `--workload prefill` makes it the headline instead.
+
 With N GPUs (torchrun) the weight columns of every layer are split across the ranks
 and the outputs are all-gathered over NCCL inside the timed region (strong scaling).
 `--impl reference` times the reference's CPU implementation of the same workload.
@@ -52,6 +56,16 @@ def peaks():
             d = json.load(f)
         return d["hbm_gbs"], "measured"
     return 6650.0, "fallback"
+
+
+def peaks_tensor():
+    """Dense bf16 GEMM peak: the sustained figure (the GEMMs run back to back for a whole step)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured sustained"
+    return 1400.0, "fallback sustained"
 
 
 def profile_traffic():
@@ -181,6 +195,91 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- prefill
+PREFILL_M = 2048
+
+
+def prefill_setup(tl, synth, dev):
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    layers = []
+    for K, N in SHAPES:
+        rng = np.random.default_rng(K * 3 + N)
+        B = torch.from_numpy(synth.pack_int2(synth.ternary(rng, K, N)).view(np.int32)).to(dev)
+        S = (torch.rand(K // 128, N, generator=g, device=dev) * 0.04 + 0.01).half()
+        A = torch.randn(PREFILL_M, K, generator=g, device=dev).half()
+        C = torch.empty(PREFILL_M, N, dtype=torch.float16, device=dev)
+        layers.append(dict(K=K, N=N, A=A, B=B, S=S, C=C))
+    return layers
+
+
+def prefill_step(tl, L, layers, sp):
+    for ly in layers:
+        st = L.ternocl_int2_upcvt(ly["A"].data_ptr(), ly["B"].data_ptr(), ly["S"].data_ptr(), ly["C"].data_ptr(),
+                                  None, None, PREFILL_M, ly["N"], ly["K"], 0, 0, 0, tl.ALGO_GEMM, None, 0, sp)
+        if st != 0:
+            raise tl.TernoclError("ternocl_int2_upcvt", st)
+
+
+def prefill_measure(tl, synth, dev, steps, warmup, profile_range=False):
+    """M=2048 int2 prefill GEMMs over the four shapes: (TFLOP/s, ms per step, launches)."""
+    import torch
+    L = tl.lib()
+    layers = prefill_setup(tl, synth, dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    for _ in range(warmup):
+        prefill_step(tl, L, layers, sp)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if profile_range:
+        torch.cuda.cudart().cudaProfilerStart()
+    ev0.record(stream)
+    for _ in range(steps):
+        prefill_step(tl, L, layers, sp)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if profile_range:
+        torch.cuda.cudart().cudaProfilerStop()
+    ms = ev0.elapsed_time(ev1) / steps
+    flops = sum(2.0 * PREFILL_M * N * K for K, N in SHAPES)
+    return flops / (ms * 1e-3) / 1e12, ms, steps * len(layers)
+
+
+def run_prefill(args, tl, synth, dev, world, rank, local):
+    """--workload prefill: the M=2048 GEMMs as the headline (replicas on N GPUs: weak scaling)."""
+    import torch
+    import torch.distributed as dist
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        tf, ms, launches = prefill_measure(tl, synth, dev, args.steps, args.warmup, args.profile_range)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = sum(2.0 * PREFILL_M * N * K for K, N in SHAPES)
+    value = world * flops / (ms * 1e-3) / 1e12
+    pk = peaks_tensor()
+    if rank == 0:
+        line = {"metric": "M=2048 int2 fp16 prefill TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": "int2_fp16_upcvt prefill GEMM (M-tiled), M=2048, llama3-8b shapes",
+                           "M": PREFILL_M, "shapes_KxN": SHAPES,
+                           "l2": "inputs larger than L2: one step touches ~340 MB (A, B, S, C of 4 shapes)",
+                           "parallelism": "replicas x%d" % world if world > 1 else "single GPU"},
+                "roofline": {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": pk[0],
+                             "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / pk[0], "peak_kind": pk[1],
+                             "kernel": "gemm_kernel<Int2Gemm>", "traffic": None},
+                "gpu_launches": launches, "clocks": clk.summary(), "cpu_baseline": None}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -192,6 +291,10 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: the headline M=1 GEMV sweep (+ prefill as a secondary figure); "
+                         "prefill: the M=2048 GEMMs alone")
+    ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--sets", type=int, default=0,
                     help="weight sets to rotate (default: enough for %.0f GiB)" % WEIGHTS_GIB)
     args = ap.parse_args()
@@ -214,6 +317,8 @@ def main():
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     tl.set_option(tl.OPT_PDL, 0 if args.no_pdl else 1)
+    if args.workload == "prefill":
+        return run_prefill(args, tl, synth, dev, world, rank, local)
 
     # per-rank column slices (multiples of 16)
     def cols(N):
@@ -344,6 +449,15 @@ def main():
         v, cores, kind, desc = CpuReference().sample()
         cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc}
 
+    secondary = None
+    if world == 1 and not args.no_secondary:
+        tf, pms, _ = prefill_measure(tl, synth, dev, steps=min(args.steps, 20), warmup=3)
+        pk = peaks_tensor()
+        secondary = {"prefill": {"metric": "M=2048 int2 fp16 prefill TFLOP/s (tcgen05 GEMM)", "value": tf,
+                                 "unit": "TFLOP/s", "ms_per_step": pms, "M": PREFILL_M, "shapes_KxN": SHAPES,
+                                 "roofline": {"bound": "tensor", "achieved": tf, "peak": pk[0], "unit": "TFLOP/s",
+                                              "frac": tf / pk[0], "peak_kind": pk[1]}}}
+
     if rank == 0:
         tr = profile_traffic()
         line = {
@@ -367,6 +481,8 @@ def main():
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
+        if secondary:
+            line["secondary"] = secondary
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])

@@ -68,7 +68,8 @@ const char *ternocl_status_string(int status);
 const char *ternocl_last_error(void);
 /* Device-side error word of the current device (synchronous read): bit 0 = a bounded
  * wait inside a kernel gave up (the kernel returned without hanging; its outputs are
- * invalid).  reset != 0 clears it.  Returns -1 if it cannot be read. */
+ * invalid); bit 1 = ternocl_moe_route met an expert id outside [0, E) (that row was
+ * left out).  reset != 0 clears it.  Returns -1 if it cannot be read. */
 int ternocl_device_error(int reset);
 
 /* Process-wide options.
@@ -77,8 +78,11 @@ int ternocl_device_error(int reset);
  *    stream.  Activations and workspaces are only touched after the previous
  *    kernel has completed; weights (B, S, SR) are read EARLY, so with this option
  *    on they must not be written by the immediately preceding kernel of the stream.
- * Returns the previous value, or -1 for an unknown option. */
-typedef enum { TERNOCL_OPT_PDL = 1 } ternocl_option;
+ *  TERNOCL_OPT_GEMM_TILE_M (default 0 = chosen per shape): rows of a prefill GEMM
+ *    CTA tile, 128 or 256 (no counterpart in the reference, whose tiles are -D
+ *    options of its kernels).
+ * Returns the previous value, or -1 for an unknown option or value. */
+typedef enum { TERNOCL_OPT_PDL = 1, TERNOCL_OPT_GEMM_TILE_M = 2 } ternocl_option;
 int ternocl_set_option(int option, int value);
 
 /* Workspace (device scratch) a call may use for its cross-CTA split-K partial sums

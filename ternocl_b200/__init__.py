@@ -13,6 +13,7 @@ FP16, BF16 = 0, 1
 POSTOP_NONE, POSTOP_SILU_MUL, POSTOP_ADD, POSTOP_BIAS, POSTOP_SIGMOID = range(5)
 ALGO_AUTO, ALGO_GEMV, ALGO_GEMM, ALGO_GEMV_TMEM = 0, 1, 2, 3
 OPT_PDL = 1
+OPT_GEMM_TILE_M = 2
 
 
 def _torch():
@@ -217,3 +218,54 @@ def hadamard_fwht(x, hb, signs=None, out=None, stream=None):
     call("ternocl_hadamard_fwht", _ptr(x), _ptr(signs), _ptr(y), rows, K, int(hb), int(signs is not None),
          dtype_code(x), _stream(stream))
     return y
+
+
+def moe_rows_per_tile():
+    return lib().ternocl_moe_rows_per_tile()
+
+
+def moe_route(ids, num_experts, stream=None):
+    """ids int32 [G] (expert of routed row g = t*topk + j) -> (meta [2E+2], perm [G], inv [G])."""
+    torch = _torch()
+    _check_cuda(ids)
+    G = ids.numel()
+    meta = torch.empty(2 * num_experts + 2, dtype=torch.int32, device=ids.device)
+    perm = torch.empty(G, dtype=torch.int32, device=ids.device)
+    inv = torch.empty(G, dtype=torch.int32, device=ids.device)
+    call("ternocl_moe_route", _ptr(ids), _ptr(meta), _ptr(perm), _ptr(inv), G, int(num_experts),
+         moe_rows_per_tile(), _stream(stream))
+    return meta, perm, inv
+
+
+def moe_gather(X, perm, topk, out=None, stream=None):
+    """Xs[p] = X[perm[p] / topk]."""
+    torch = _torch()
+    _check_cuda(X, perm, out)
+    G = perm.numel()
+    K = X.shape[1]
+    Xs = torch.empty(G, K, dtype=X.dtype, device=X.device) if out is None else out
+    call("ternocl_moe_gather", _ptr(X), _ptr(perm), _ptr(Xs), G, K, int(topk), _stream(stream))
+    return Xs
+
+
+def moe_gemm(meta, A, B_all, S_all, num_experts, postop=0, out_f32=False, other=None, out=None, stream=None):
+    """Per-expert C[p] = epi(A[p] @ dequant(B_all[e], S_all[e])) for the sorted rows p of expert e.
+    A [G, K]; B_all int32 [E, K/16, N]; S_all [E, K/128, N]; other [G, N] for POSTOP 1/2."""
+    _check_cuda(meta, A, B_all, S_all, other, out)
+    G, K = A.shape
+    N = B_all.shape[-1]
+    C = _out(G, N, A, out_f32, out)
+    call("ternocl_moe_gemm", _ptr(meta), _ptr(A), _ptr(B_all), _ptr(S_all), _ptr(C), _ptr(other), G, N, K,
+         int(num_experts), dtype_code(A), int(postop), int(bool(out_f32)), _stream(stream))
+    return C
+
+
+def moe_combine(Y, inv, RW, T, topk, out=None, stream=None):
+    """O[t] = sum_j RW[t*topk+j] * Y[inv[t*topk+j]]; Y fp32 [G, N], RW [G] fp16/bf16."""
+    torch = _torch()
+    _check_cuda(Y, inv, RW, out)
+    N = Y.shape[1]
+    O = torch.empty(T, N, dtype=RW.dtype, device=Y.device) if out is None else out
+    call("ternocl_moe_combine", _ptr(Y), _ptr(inv), _ptr(RW), _ptr(O), int(T), N, int(topk), dtype_code(RW),
+         _stream(stream))
+    return O

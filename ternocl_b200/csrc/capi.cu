@@ -164,6 +164,12 @@ int ternocl_set_option(int option, int value) {
         options().pdl = value ? 1 : 0;
         return old;
     }
+    if (option == TERNOCL_OPT_GEMM_TILE_M) {
+        if (value != 0 && value != 128 && value != 256) return -1;
+        const int old = options().gemm_tile_m;
+        options().gemm_tile_m = value;
+        return old;
+    }
     return -1;
 }
 
@@ -182,6 +188,8 @@ int ternocl_device_error(int reset) {
     if (read_device_error_gemv_tc(&t, reset) != cudaSuccess) return -1;
     v |= t;
     if (read_device_error_gemm_tc(&t, reset) != cudaSuccess) return -1;
+    v |= t;
+    if (read_device_error_moe(&t, reset) != cudaSuccess) return -1;
     v |= t;
     return (int)v;
 }
@@ -317,21 +325,45 @@ int ternocl_int2_int8_group_dots(const int8_t *Aq, const uint32_t *B, int32_t *D
     return cuda_status(group_dots_launch(Aq, B, Dots, M, N, K, (cudaStream_t)stream));
 }
 
-// ---- entry points whose kernels are not built yet: report UNSUPPORTED ----------
 int ternocl_moe_rows_per_tile(void) { return 128; }
-int ternocl_moe_route(const int32_t *, int32_t *, int32_t *, int32_t *, int, int, int, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+
+int ternocl_moe_route(const int32_t *ids, int32_t *meta, int32_t *perm, int32_t *inv, int G, int E, int rows_per_tile,
+                      void *stream) {
+    if (G < 0 || E < 1 || E > 1024) return TERNOCL_ERR_SHAPE;
+    if (rows_per_tile != ternocl_moe_rows_per_tile()) return TERNOCL_ERR_ARG;
+    if (!meta || (G > 0 && (!ids || !perm || !inv))) return TERNOCL_ERR_ARG;
+    return cuda_status(moe_route_launch(ids, meta, perm, inv, G, E, rows_per_tile, (cudaStream_t)stream));
 }
-int ternocl_moe_gather(const void *, const int32_t *, void *, int, int, int, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+
+int ternocl_moe_gather(const void *X, const int32_t *perm, void *Xs, int G, int K, int topk, void *stream) {
+    if (G < 0 || K <= 0 || K % 8 || topk < 1) return TERNOCL_ERR_SHAPE;
+    if (G == 0) return TERNOCL_OK;
+    if (!X || !perm || !Xs || !aligned(X, 16) || !aligned(Xs, 16)) return TERNOCL_ERR_ARG;
+    return cuda_status(moe_gather_launch(X, perm, Xs, G, K, topk, (cudaStream_t)stream));
 }
-int ternocl_moe_gemm(const int32_t *, const void *, const uint32_t *, const void *, void *,
-                     const void *, int, int, int, int, int, int, int, void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+
+int ternocl_moe_gemm(const int32_t *meta, const void *A_all, const uint32_t *B_all, const void *S_all, void *C_all,
+                     const void *Other_all, int G, int N, int K, int E, int dtype, int postop, int out_f32,
+                     void *stream) {
+    int st = check_gemm_common(A_all, B_all, S_all, C_all, Other_all, nullptr, G, N, K, dtype, postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (postop == 3) return TERNOCL_ERR_ARG;  // no bias in the MoE GEMM (int2_moe_prefill.cl:95)
+    if (!meta || E < 1 || E > 1024) return TERNOCL_ERR_ARG;
+    if (G == 0) return TERNOCL_OK;
+    GemvArgs a;
+    a.A = A_all; a.B = B_all; a.S = S_all; a.C = C_all; a.Other = Other_all; a.Bias = nullptr;
+    a.M = G; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.stream = (cudaStream_t)stream;
+    return cuda_status(moe_gemm_tc_launch(a, meta, E));
 }
-int ternocl_moe_combine(const float *, const int32_t *, const void *, void *, int, int, int, int,
-                        void *) {
-    return TERNOCL_ERR_UNSUPPORTED;
+
+int ternocl_moe_combine(const float *Y, const int32_t *inv, const void *RW, void *O, int T, int N, int topk,
+                        int dtype, void *stream) {
+    if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
+    if (T < 0 || N <= 0 || N % 4 || topk < 1) return TERNOCL_ERR_SHAPE;
+    if (T == 0) return TERNOCL_OK;
+    if (!Y || !inv || !RW || !O || !aligned(Y, 16) || !aligned(O, 8)) return TERNOCL_ERR_ARG;
+    return cuda_status(moe_combine_launch(Y, inv, RW, O, T, N, topk, dtype, (cudaStream_t)stream));
 }
 
 }  // extern "C"

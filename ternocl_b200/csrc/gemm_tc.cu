@@ -7,15 +7,17 @@
 // As in the reference's GEMM the weights are upconverted to DT +-s (or 0) before the
 // MMA (exact: s is a DT value), and the products are accumulated in fp32.
 //
-// CTA tile 128 (M) x 256 (N), K in steps of 64; 320 threads in three roles:
-//   warp 0      TMA producer: A [128 x 64] through a 2-D tensor map (8 boxes of 128
-//               rows x 16 bytes = the no-swizzle K-major core-matrix layout), the
-//               packed weight rows and the scale row through 1-D bulk copies, all
-//               completing on one mbarrier per stage (4 load stages);
-//   warp 1      TMEM allocation (256 fp32 columns) and the MMA issuer: per stage four
-//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16), A and B from
-//               shared-memory descriptors, accumulator in TMEM; tcgen05.commit frees
-//               the stage and the decoded buffer;
+// CTA tile 256 (M; 128 for M <= 128 and for MoE row tiles) x 256 (N), K in steps of
+// 64; 320 threads in three roles:
+//   warp 0      TMA producer: A [rows x 64] through a 2-D tensor map (8 boxes of rows x
+//               16 bytes = the no-swizzle K-major core-matrix layout), the packed
+//               weight rows and the scale row through 1-D bulk copies, all completing
+//               on one mbarrier per stage (3-4 load stages);
+//   warp 1      TMEM allocation (256 fp32 columns per 128-row half) and the MMA
+//               issuer: per stage and half four tcgen05.mma.cta_group::1.kind::f16
+//               (M=128, N=256, K=16), A and B from shared-memory descriptors (both
+//               halves read the same decoded B), accumulators in TMEM;
+//               tcgen05.commit frees the stage and the decoded buffer;
 //   warps 2-9   decode: warp kc, lane nb turns the packed words of 8 columns
 //               (8nb..8nb+7) and 8 K rows (8kc..8kc+7 of the stage) into one 8x8
 //               core matrix of the B operand, MN-major (a core-matrix row = one K row,
@@ -42,30 +44,36 @@
 namespace ternocl {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kLoadStages = 4, kDecStages = 3;
+constexpr int BM = 128, BN = 256, BK = 64;  // BM: rows of one MMA (cta_group::1)
+constexpr int kDecStages = 3;
 constexpr int kDecWarps = 8;
 constexpr int kThreads = (2 + kDecWarps) * 32;
 // decoded B (MN-major, no swizzle): core matrix (kc, nb) at nb * kDecSBO + kc * 128;
 // the 16-byte pad in kDecSBO spreads the decode warps' stores over all banks
 constexpr int kDecLBO = 128, kDecSBO = BK / 8 * 128 + 16;  // 1040
 constexpr int kDecStageBytes = (BN / 8) * kDecSBO;         // 33280
-// A (K-major, no swizzle): box c (K = 8c .. 8c+7) = 128 rows x 16 bytes at c * 2048
-constexpr int kALBO = BM * 16, kASBO = 128;
-constexpr int kAStageBytes = BM * BK * 2;  // 16384
-constexpr int kPackStageBytes = 4096;      // int2: 4 word rows x 256 columns; int1: 2 x 256
+constexpr int kPackStageBytes = 4096;  // int2: 4 word rows x 256 columns; int1: 2 x 256
 constexpr int kScaleStageBytes = BN * 2;
-constexpr int kTmemCols = BN;
 
-struct Smem {
+// A CTA tile is HALVES x 128 rows: with two halves the decoded B tile of a stage feeds
+// two MMAs (one per 128-row half, accumulators side by side in TMEM), which halves the
+// decode work and the shared-memory traffic of B per multiply-add.
+template <int HALVES>
+struct Cfg {
+    static constexpr int kRows = BM * HALVES;
+    static constexpr int kLoadStages = HALVES == 2 ? 3 : 4;
+    // A (K-major, no swizzle): box c (K = 8c .. 8c+7) = kRows rows x 16 bytes at c * kALBO
+    static constexpr int kALBO = kRows * 16, kASBO = 128;
+    static constexpr int kAStageBytes = kRows * BK * 2;
+    static constexpr int kTmemCols = BN * HALVES;
     // decoded buffers first: every descriptor-derived address stays inside the block
     static constexpr int dec = 0;
-    static constexpr int a = dec + kDecStages * kDecStageBytes;  // 99840 (1024-aligned below)
-    static constexpr int a_al = (a + 1023) / 1024 * 1024;
-    static constexpr int pack = a_al + kLoadStages * kAStageBytes;
+    static constexpr int a = (kDecStages * kDecStageBytes + 1023) / 1024 * 1024;
+    static constexpr int pack = a + kLoadStages * kAStageBytes;
     static constexpr int scale = pack + kLoadStages * kPackStageBytes;
     static constexpr int bars = scale + kLoadStages * kScaleStageBytes;
     static constexpr int total = bars + 256;
+    static_assert(total <= 227 * 1024, "shared memory");
 };
 
 struct Params {
@@ -75,6 +83,10 @@ struct Params {
     const uint16_t *Other;
     const void *Bias;
     int M, N, K;
+    // grouped (MoE) mode: meta = [E+1 row offsets | E+1 row-tile offsets] of the rows
+    // sorted by expert; blockIdx.y is a row tile of some expert, B and S are [E, ...]
+    const int *meta;
+    int E;
 };
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -104,6 +116,7 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
 // ---- int2: [K/16, N] words, 4 word rows per stage --------------------------------
 struct Int2Gemm {
     static constexpr int kRowsPerStage = BK / 16;  // packed word rows per stage
+    static constexpr int kKPerWordRow = 16;
     __device__ static const uint32_t *row_ptr(const Params &p, int kb, int r, int n0) {
         return p.B + (size_t)(kb * kRowsPerStage + r) * p.N + n0;
     }
@@ -111,7 +124,11 @@ struct Int2Gemm {
     template <class DT>
     __device__ static void decode(const char *pack, const uint16_t *scale, int kc, int nb, uint4 out[8]) {
         const uint4 *src = reinterpret_cast<const uint4 *>(pack + (kc >> 1) * (BN * 4) + nb * 32);
-        const uint4 w0 = src[0], w1 = src[1];
+        // lanes 4..7 of each quarter-warp read their two 16-byte chunks in the other
+        // order, so that both loads touch 8 distinct 16-byte bank groups
+        const int sw = (nb >> 2) & 1;
+        const uint4 c0 = src[sw], c1 = src[sw ^ 1];
+        const uint4 w0 = sw ? c1 : c0, w1 = sw ? c0 : c1;
         const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         const uint4 sv = *reinterpret_cast<const uint4 *>(scale + nb * 8);
         const uint32_t s2[4] = {sv.x, sv.y, sv.z, sv.w};  // (s_{2i}, s_{2i+1})
@@ -132,6 +149,7 @@ struct Int2Gemm {
 // ---- int1: sel layout [K/32, N], 2 word rows per stage --------------------------
 struct Int1Gemm {
     static constexpr int kRowsPerStage = BK / 32;
+    static constexpr int kKPerWordRow = 32;
     __device__ static const uint32_t *row_ptr(const Params &p, int kb, int r, int n0) {
         return p.B + (size_t)(kb * kRowsPerStage + r) * p.N + n0;
     }
@@ -165,14 +183,36 @@ struct Int1Gemm {
     }
 };
 
-template <class Policy, class DT, int POSTOP, bool OUT_F32>
-__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tmA) {
+template <class Policy, int HALVES, class DT, int POSTOP, bool OUT_F32>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, const __grid_constant__ CUtensorMap tmA) {
+    using C = Cfg<HALVES>;
+    constexpr int kLoadStages = C::kLoadStages;
     extern __shared__ __align__(1024) char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int n0 = blockIdx.x * BN;
+    Params p = pin;
+    int m0 = blockIdx.y * C::kRows;  // first A / C row of the tile
+    int m_end = p.M;           // rows >= m_end are not stored
+    if (p.meta) {
+        // the tile's expert: the last one whose first row tile is <= this tile
+        // (int2_moe_prefill.cl:80-88); meta comes from the routing kernel
+        pdl_wait();
+        const int tile = blockIdx.y, E = p.E;
+        if (tile >= p.meta[2 * E + 1]) return;
+        int lo = 0, hi = E - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.meta[E + 1 + mid] <= tile) lo = mid;
+            else hi = mid - 1;
+        }
+        m0 = p.meta[lo] + (tile - p.meta[E + 1 + lo]) * BM;
+        m_end = p.meta[lo + 1];
+        p.B += (size_t)lo * (p.K / Policy::kKPerWordRow) * p.N;
+        p.S += (size_t)lo * (p.K / kGS) * p.N;
+    }
     const int nk = p.K / BK;
     const int ncols = min(BN, p.N - n0);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::bars);
     uint64_t *load_empty = full + kLoadStages;
     uint64_t *dec_full = load_empty + kLoadStages;
     uint64_t *dec_empty = dec_full + kDecStages;
@@ -191,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const
         tc::mbar_init(acc_full, 1);
         tc::fence_mbar_init();
     }
-    if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 1) tc::tmem_alloc(tmem_slot, C::kTmemCols);
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -206,15 +246,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % kLoadStages;
                 if (kb >= kLoadStages && !tc::mbar_wait(&load_empty[s], ((kb / kLoadStages) - 1) & 1)) break;
-                tc::mbar_expect_tx(&full[s], kAStageBytes + pack_bytes + scale_bytes);
-                char *a = smem + Smem::a_al + s * kAStageBytes;
+                tc::mbar_expect_tx(&full[s], C::kAStageBytes + pack_bytes + scale_bytes);
+                char *a = smem + C::a + s * C::kAStageBytes;
 #pragma unroll
-                for (int c = 0; c < BK / 8; ++c) tma_load_2d(a + c * kALBO, &tmA, kb * BK + 8 * c, m0, &full[s]);
-                char *pk = smem + Smem::pack + s * kPackStageBytes;
+                for (int c = 0; c < BK / 8; ++c) tma_load_2d(a + c * C::kALBO, &tmA, kb * BK + 8 * c, m0, &full[s]);
+                char *pk = smem + C::pack + s * kPackStageBytes;
                 for (int r = 0; r < Policy::kRowsPerStage; ++r)
                     tc::bulk_g2s(pk + r * (BN * 4), Policy::row_ptr(p, kb, r, n0), pack_bytes / Policy::kRowsPerStage,
                                  &full[s]);
-                tc::bulk_g2s(smem + Smem::scale + s * kScaleStageBytes, p.S + (size_t)(kb * BK / kGS) * p.N + n0,
+                tc::bulk_g2s(smem + C::scale + s * kScaleStageBytes, p.S + (size_t)(kb * BK / kGS) * p.N + n0,
                              scale_bytes, &full[s]);
                 ++issued;
             }
@@ -231,13 +271,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const
                 if (!tc::mbar_wait(&full[s], (kb / kLoadStages) & 1)) break;
                 if (!tc::mbar_wait(&dec_full[d], (kb / kDecStages) & 1)) break;
                 tc::fence_after_sync();
-                const uint32_t a = tc::smem_addr(smem + Smem::a_al + s * kAStageBytes);
-                const uint32_t b = tc::smem_addr(smem + Smem::dec + d * kDecStageBytes);
+                const uint32_t a = tc::smem_addr(smem + C::a + s * C::kAStageBytes);
+                const uint32_t b = tc::smem_addr(smem + C::dec + d * kDecStageBytes);
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t ad = tc::sdesc_kmajor_noswz(a + kk * 2 * kALBO, kALBO, kASBO);
                     const uint64_t bd = tc::sdesc_kmajor_noswz(b + kk * 2 * kDecLBO, kDecLBO, kDecSBO);
-                    mma_ss_f16(tmem, ad, bd, idesc, (kb | kk) != 0);
+#pragma unroll
+                    for (int h = 0; h < HALVES; ++h) {
+                        // rows 128h .. 128h+127 of the A stage: 16 core matrices from h * 2048
+                        const uint64_t ad = tc::sdesc_kmajor_noswz(a + kk * 2 * C::kALBO + h * BM * 16, C::kALBO,
+                                                                   C::kASBO);
+                        mma_ss_f16(tmem + h * BN, ad, bd, idesc, (kb | kk) != 0);
+                    }
                 }
                 tc::mma_commit(&load_empty[s]);
                 tc::mma_commit(&dec_empty[d]);
@@ -252,10 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const
             if (!tc::mbar_wait(&full[s], (kb / kLoadStages) & 1)) break;
             if (kb >= kDecStages && !tc::mbar_wait(&dec_empty[d], ((kb / kDecStages) - 1) & 1)) break;
             uint4 rows[8];
-            Policy::template decode<DT>(smem + Smem::pack + s * kPackStageBytes,
-                                        reinterpret_cast<const uint16_t *>(smem + Smem::scale + s * kScaleStageBytes),
+            Policy::template decode<DT>(smem + C::pack + s * kPackStageBytes,
+                                        reinterpret_cast<const uint16_t *>(smem + C::scale + s * kScaleStageBytes),
                                         kc, nb, rows);
-            char *dst = smem + Smem::dec + d * kDecStageBytes + nb * kDecSBO + kc * 128;
+            char *dst = smem + C::dec + d * kDecStageBytes + nb * kDecSBO + kc * 128;
 #pragma unroll
             for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4 *>(dst + r * 16) = rows[r];
             tc::fence_proxy_async_smem();
@@ -268,14 +313,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const
         if (tc::mbar_wait(acc_full, 0)) {
             tc::fence_after_sync();
             const int quad = warp & 3, half = kc >> 2;
-            const int m = m0 + 32 * quad + lane;
 #pragma unroll 1
-            for (int c = 0; c < BN / 2 / 16; ++c) {
-                const int col = half * (BN / 2) + 16 * c;
+            for (int c = 0; c < HALVES * BN / 2 / 16; ++c) {
+                const int h = c / (BN / 2 / 16);  // 128-row half of the tile
+                const int col = half * (BN / 2) + 16 * (c % (BN / 2 / 16));
+                const int m = m0 + h * BM + 32 * quad + lane;
                 float v[16];
-                tc::tmem_ld<16>(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)col, v);
+                tc::tmem_ld<16>(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(h * BN + col), v);
                 tc::tmem_wait_ld();
-                if (m < p.M && col < ncols) {
+                if (m < m_end && col < ncols) {
 #pragma unroll
                     for (int i = 0; i < 16; i += 2)
                         epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, n0 + col + i, v[i], v[i + 1]);
@@ -288,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params p, const
     __syncthreads();
     if (warp == 1) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, kTmemCols);
+        tc::tmem_dealloc(tmem, C::kTmemCols);
     }
 }
 
@@ -311,13 +357,13 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// A [M, K] DT row-major; boxes of 128 rows x 8 elements, rows past M read as zero
-static cudaError_t make_map_a(CUtensorMap *map, const void *A, int M, int K, bool bf16) {
+// A [M, K] DT row-major; boxes of box_rows rows x 8 elements, rows past M read as zero
+static cudaError_t make_map_a(CUtensorMap *map, const void *A, int M, int K, bool bf16, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {8, BM};
+    const cuuint32_t box[2] = {8, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                           const_cast<void *>(A), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -326,12 +372,14 @@ static cudaError_t make_map_a(CUtensorMap *map, const void *A, int M, int K, boo
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <class Policy>
-cudaError_t launch_policy(const GemvArgs &a) {
+template <class Policy, int HALVES>
+cudaError_t launch_policy(const GemvArgs &a, const int *meta = nullptr, int E = 0) {
     CUtensorMap map;
-    cudaError_t e = make_map_a(&map, a.A, a.M, a.K, a.dtype == TERNOCL_BF16);
+    cudaError_t e = make_map_a(&map, a.A, a.M, a.K, a.dtype == TERNOCL_BF16, Cfg<HALVES>::kRows);
     if (e != cudaSuccess) return e;
     Params p;
+    p.meta = meta;
+    p.E = E;
     p.B = a.B;
     p.S = (const uint16_t *)a.S;
     p.C = a.C;
@@ -342,18 +390,46 @@ cudaError_t launch_policy(const GemvArgs &a) {
     p.K = a.K;
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
-        auto kern = gemm_kernel<Policy, DT, decltype(po)::value, decltype(of)::value>;
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total);
+        auto kern = gemm_kernel<Policy, HALVES, DT, decltype(po)::value, decltype(of)::value>;
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<HALVES>::total);
         if (err != cudaSuccess) return err;
-        const dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
-        return launch_kernel(kern, grid, dim3(kThreads), (size_t)Smem::total, a.stream, p, map);
+        // grouped: every expert adds at most one partial row tile
+        const int rows = Cfg<HALVES>::kRows;
+        const int tiles = (a.M + rows - 1) / rows + (meta ? E : 0);
+        const dim3 grid((a.N + BN - 1) / BN, tiles);
+        return launch_kernel(kern, grid, dim3(kThreads), (size_t)Cfg<HALVES>::total, a.stream, p, map);
     });
 }
 
 }  // namespace gemm
 
-cudaError_t int2_gemm_tc_launch(const GemvArgs &a) { return gemm::launch_policy<gemm::Int2Gemm>(a); }
-cudaError_t int1_gemm_tc_launch(const GemvArgs &a) { return gemm::launch_policy<gemm::Int1Gemm>(a); }
+namespace gemm {
+// 128- or 256-row tiles: one CTA per SM, so a grid runs in ceil(tiles / SMs) waves; a
+// 256-row tile does twice the work of a 128-row one in ~1.6x the time (measured on
+// B200), so pick the shape with fewer wave-weighted units.  MoE tiles are 128 rows.
+static bool use_256_rows(int M, int N) {
+    if (options().gemm_tile_m) return options().gemm_tile_m == 256;
+    if (M <= BM) return false;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long nt = (N + BN - 1) / BN;
+    const long long w1 = ((M + BM - 1) / BM * nt + sms - 1) / sms;
+    const long long w2 = ((M + 2 * BM - 1) / (2 * BM) * nt + sms - 1) / sms;
+    return w2 * 16 < w1 * 10;
+}
+}  // namespace gemm
+
+cudaError_t int2_gemm_tc_launch(const GemvArgs &a) {
+    return gemm::use_256_rows(a.M, a.N) ? gemm::launch_policy<gemm::Int2Gemm, 2>(a)
+                                        : gemm::launch_policy<gemm::Int2Gemm, 1>(a);
+}
+cudaError_t int1_gemm_tc_launch(const GemvArgs &a) {
+    return gemm::use_256_rows(a.M, a.N) ? gemm::launch_policy<gemm::Int1Gemm, 2>(a)
+                                        : gemm::launch_policy<gemm::Int1Gemm, 1>(a);
+}
+cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E) {
+    return gemm::launch_policy<gemm::Int2Gemm, 1>(a, meta, E);
+}
 cudaError_t read_device_error_gemm_tc(unsigned *out, int reset) { return tc::read_tu_error(out, reset); }
 
 }  // namespace ternocl

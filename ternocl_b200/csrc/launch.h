@@ -15,7 +15,8 @@ struct BF16;
 
 // Process-wide options (ternocl_set_option).
 struct Options {
-    int pdl = 0;  // launch with programmatic stream serialization
+    int pdl = 0;          // launch with programmatic stream serialization
+    int gemm_tile_m = 0;  // prefill GEMM CTA rows: 0 = per shape, 128 or 256
 };
 Options &options();
 
@@ -126,6 +127,16 @@ cudaError_t read_device_error_gemv_tc(unsigned *out, int reset);
 cudaError_t int2_gemm_tc_launch(const GemvArgs &a);
 cudaError_t int1_gemm_tc_launch(const GemvArgs &a);
 cudaError_t read_device_error_gemm_tc(unsigned *out, int reset);
+// grouped (MoE) int2 GEMM over the rows of meta's experts; a.M = G rows
+cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E);
+// MoE routing / gather / combine (moe.cu)
+size_t moe_route_smem(int E);
+cudaError_t moe_route_launch(const int *ids, int *meta, int *perm, int *inv, int G, int E, int rpt,
+                             cudaStream_t st);
+cudaError_t moe_gather_launch(const void *X, const int *perm, void *Xs, int G, int K, int topk, cudaStream_t st);
+cudaError_t moe_combine_launch(const float *Y, const int *inv, const void *RW, void *O, int T, int N, int topk,
+                               int dtype, cudaStream_t st);
+cudaError_t read_device_error_moe(unsigned *out, int reset);
 // M from which TERNOCL_ALGO_AUTO picks the GEMM (int2_fp16_upcvt/main.cpp:160)
 constexpr int kGemmMinM = 64;
 // split-K factor the register-decode GEMV's planner picks when a workspace exists

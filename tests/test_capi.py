@@ -47,6 +47,34 @@ def test_shape_and_argument_checks_without_gpu():
     assert L.ternocl_int8_ldsa(1) == 32 and L.ternocl_int8_ldsa(33) == 64
 
 
+def test_more_host_checks_without_gpu():
+    L = _lib.lib()
+    p = ctypes.c_void_p(64)
+    # s8 x s2: qmode 0/1 only; quant_a needs K % 128
+    assert L.ternocl_int2_int8(p, p, p, p, p, p, None, None, 1, 48, 128, 0, 0, 0, 3, 0, None) == 2
+    assert L.ternocl_int8_quant_a(p, p, None, 1, 200, 0, None) == 1
+    # BITCOS: K % (64 ls), slice ranks needed for ls > 1
+    assert L.ternocl_bitcos_upcvt(p, p, p, p, 3, p, None, None, 1, 48, 256, 0, 0, 0, 0, None) == 1
+    assert L.ternocl_bitcos_upcvt(p, p, p, None, 2, p, None, None, 1, 48, 256, 0, 0, 0, 0, None) == 2
+    # FWHT: HB a power of two in [256, 4096] dividing K
+    assert L.ternocl_hadamard_fwht(p, None, p, 1, 5376, 1024, 0, 0, None) == 1
+    assert L.ternocl_hadamard_fwht(p, None, p, 1, 4096, 8192, 0, 0, None) == 1
+    # MoE: rows per tile is the GEMM's, no bias epilogue, E range
+    assert L.ternocl_moe_route(p, p, p, p, 8, 4, 64, None) == 2
+    assert L.ternocl_moe_route(p, p, p, p, 8, 0, 128, None) == 1
+    assert L.ternocl_moe_gemm(p, p, p, p, p, None, 8, 48, 128, 4, 0, 3, 0, None) == 2
+    assert L.ternocl_moe_combine(p, p, p, p, 2, 50, 8, 0, None) == 1
+
+
+def test_options():
+    L = _lib.lib()
+    old = L.ternocl_set_option(1, 1)
+    assert L.ternocl_set_option(1, old) == 1
+    assert L.ternocl_set_option(2, 100) == -1  # GEMM tile rows: 0, 128 or 256
+    assert L.ternocl_set_option(2, 256) == 0 and L.ternocl_set_option(2, 0) == 256
+    assert L.ternocl_set_option(99, 1) == -1
+
+
 def test_host_bitcos_packer_roundtrip():
     L = _lib.lib()
     rng = np.random.default_rng(3)

@@ -24,9 +24,17 @@ def run_int2(tl, c, bf16, postop, out_f32, algo):
     return host_dt(tl.int2_upcvt(A, B, S, postop=postop, out_f32=out_f32, other=other, bias=bias, algo=algo))
 
 
+@pytest.fixture(params=[0, 128, 256], ids=["tile_auto", "tile128", "tile256"])
+def tile_m(request, tl):
+    """Every prefill test runs with the per-shape tile choice and with each tile forced."""
+    old = tl.set_option(tl.OPT_GEMM_TILE_M, request.param)
+    yield request.param
+    tl.set_option(tl.OPT_GEMM_TILE_M, old)
+
+
 @pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("M,K,N", SHAPES)
-def test_int2_gemm_parity(cuda, tl, M, K, N, bf16):
+def test_int2_gemm_parity(cuda, tl, tile_m, M, K, N, bf16):
     c = int2_case(600 + M + K + N, M, K, N, bf16)
     gold = int2_gold_out(c, M, K, N, bf16, 0, False)
     check_output(run_int2(tl, c, bf16, 0, False, tl.ALGO_GEMM), gold, bf16, False,
@@ -37,7 +45,7 @@ def test_int2_gemm_parity(cuda, tl, M, K, N, bf16):
 @pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("postop", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("out_f32", [False, True])
-def test_int2_gemm_epilogues(cuda, tl, bf16, postop, out_f32):
+def test_int2_gemm_epilogues(cuda, tl, tile_m, bf16, postop, out_f32):
     M, K, N = 192, 512, 512
     c = int2_case(80 + postop, M, K, N, bf16, postop, out_f32)
     gold = int2_gold_out(c, M, K, N, bf16, postop, out_f32)
@@ -45,7 +53,7 @@ def test_int2_gemm_epilogues(cuda, tl, bf16, postop, out_f32):
                  "postop=%d out_f32=%d" % (postop, out_f32))
 
 
-def test_int2_gemm_decode_bit_exact(cuda, tl):
+def test_int2_gemm_decode_bit_exact(cuda, tl, tile_m):
     # A = identity: C = the upconverted weights code * S exactly, every 2-bit code
     K, N = 256, 512
     rng = np.random.default_rng(4)
@@ -59,7 +67,7 @@ def test_int2_gemm_decode_bit_exact(cuda, tl):
     assert np.array_equal(out, want)
 
 
-def test_int2_gemm_deterministic(cuda, tl):
+def test_int2_gemm_deterministic(cuda, tl, tile_m):
     M, K, N = 256, 1024, 768
     c = int2_case(11, M, K, N, 1)
     outs = [run_int2(tl, c, 1, 0, False, tl.ALGO_GEMM) for _ in range(3)]
@@ -87,7 +95,7 @@ def run_int1(tl, c, bf16, postop, out_f32, algo):
 
 @pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("M,K,N", SHAPES)
-def test_int1_gemm_parity(cuda, tl, M, K, N, bf16):
+def test_int1_gemm_parity(cuda, tl, tile_m, M, K, N, bf16):
     c = int1_case(700 + M + K + N, M, K, N, bf16)
     acc = orc.int1_gold(c["A"], c["Bpc"], c["S"], M, K, N, bf16)
     gold = orc.epilogue(0, False, acc, None, None, M, N, bf16)
@@ -96,7 +104,7 @@ def test_int1_gemm_parity(cuda, tl, M, K, N, bf16):
 
 
 @pytest.mark.parametrize("postop,out_f32", [(1, False), (3, True), (4, False)])
-def test_int1_gemm_epilogues(cuda, tl, postop, out_f32):
+def test_int1_gemm_epilogues(cuda, tl, tile_m, postop, out_f32):
     M, K, N = 128, 512, 256
     c = int1_case(90 + postop, M, K, N, 0, postop, out_f32)
     acc = orc.int1_gold(c["A"], c["Bpc"], c["S"], M, K, N, 0)
@@ -104,7 +112,7 @@ def test_int1_gemm_epilogues(cuda, tl, postop, out_f32):
     check_output(run_int1(tl, c, 0, postop, out_f32, tl.ALGO_AUTO), gold, 0, out_f32, "postop=%d" % postop)
 
 
-def test_int1_gemm_decode_bit_exact(cuda, tl):
+def test_int1_gemm_decode_bit_exact(cuda, tl, tile_m):
     K, N = 256, 512
     rng = np.random.default_rng(5)
     Bpc = rng.integers(0, 1 << 32, size=(K // 32, N), dtype=np.uint64).astype(np.uint32)

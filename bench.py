@@ -8,7 +8,8 @@ scales uniform [0.01, 0.05], activations N(0, 1); distinct weight sets rotated s
 that more than 2 GiB of weights stream (every call reads its weights from HBM, none
 from the 126 MB L2).  One step = one GEMV per shape, each on the next weight set.
 
-  value      weight-stream GB/s (B + S bytes / time, all ranks), inputs resident in HBM
+  value      weight-stream GB/s (B + S bytes / time, all ranks), inputs resident in HBM;
+             (host launches with programmatic dependent launch; --graph: one CUDA graph)
   e2e        same metric through the C ABI with host buffers: activations copied
              host->device and outputs device->host inside the timed region
   roofline   the GEMV kernel's weight bytes per launch / its mean launch time vs the
@@ -247,6 +248,157 @@ def prefill_measure(tl, synth, dev, steps, warmup, profile_range=False):
     return flops / (ms * 1e-3) / 1e12, ms, steps * len(layers)
 
 
+# ----------------------------------------------------------------------------- MoE prefill
+MOE = dict(T=4096, H=2048, I=768, E=128, topk=8)
+
+
+def moe_setup(tl, synth, dev, seed=5):
+    """C5: 4096 tokens, 128 experts, top-8 distinct uniform, gates softmax(N(0,1)),
+    ternary int2 gate/up [E, H/16, I] and down [E, I/16, H], scales U(0.01, 0.05)."""
+    import torch
+    T, H, I, E, topk = MOE["T"], MOE["H"], MOE["I"], MOE["E"], MOE["topk"]
+    rng = np.random.default_rng(seed)
+    ids = np.argsort(rng.random((T, E)), axis=1)[:, :topk].astype(np.int32).reshape(-1)
+    g = rng.standard_normal((T, topk))
+    rw = (np.exp(g) / np.exp(g).sum(1, keepdims=True)).reshape(-1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+
+    shifts = (2 * torch.arange(16, device=dev, dtype=torch.int64)).view(1, 16, 1)
+
+    def weights(K, N):
+        B = torch.empty(E, K // 16, N, dtype=torch.int32, device=dev)
+        for e in range(E):  # uniform {0, +1, -1} -> codes {0, 1, 3}, 16 per word
+            codes = torch.randint(0, 3, (K // 16, 16, N), generator=gen, device=dev, dtype=torch.int64)
+            codes = torch.where(codes == 2, torch.full_like(codes, 3), codes)
+            w = (codes << shifts).sum(dim=1)
+            B[e] = torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)
+        S = (torch.rand(E, K // 128, N, generator=gen, device=dev) * 0.04 + 0.01).half()
+        return B, S
+
+    Bg, Sg = weights(H, I)
+    Bu, Su = weights(H, I)
+    Bd, Sd = weights(I, H)
+    G = T * topk
+    return dict(ids=torch.from_numpy(ids).to(dev), RW=torch.from_numpy(rw).half().to(dev),
+                X=torch.randn(T, H, generator=gen, device=dev).half(), Bg=Bg, Sg=Sg, Bu=Bu, Su=Su, Bd=Bd, Sd=Sd,
+                Xs=torch.empty(G, H, dtype=torch.float16, device=dev),
+                up=torch.empty(G, I, dtype=torch.float16, device=dev),
+                Hh=torch.empty(G, I, dtype=torch.float16, device=dev),
+                Y=torch.empty(G, H, dtype=torch.float32, device=dev),
+                O=torch.empty(T, H, dtype=torch.float16, device=dev))
+
+
+def moe_layer(tl, m, stream=None):
+    """route -> gather -> up, gate (SiLU-mul with up), down (fp32) -> combine: 7 launches."""
+    E, topk = MOE["E"], MOE["topk"]
+    meta, perm, inv = tl.moe_route(m["ids"], E, stream=stream)
+    tl.moe_gather(m["X"], perm, topk, out=m["Xs"], stream=stream)
+    tl.moe_gemm(meta, m["Xs"], m["Bu"], m["Su"], E, out=m["up"], stream=stream)
+    tl.moe_gemm(meta, m["Xs"], m["Bg"], m["Sg"], E, postop=1, other=m["up"], out=m["Hh"], stream=stream)
+    tl.moe_gemm(meta, m["Hh"], m["Bd"], m["Sd"], E, out_f32=True, out=m["Y"], stream=stream)
+    tl.moe_combine(m["Y"], inv, m["RW"], MOE["T"], topk, out=m["O"], stream=stream)
+
+
+def moe_measure(tl, synth, dev, steps, warmup):
+    """(tokens/s, TFLOP/s, ms per layer) of the C5 MoE prefill layer."""
+    import torch
+    m = moe_setup(tl, synth, dev)
+    for _ in range(warmup):
+        moe_layer(tl, m)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        moe_layer(tl, m)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    G = MOE["T"] * MOE["topk"]
+    flops = 2.0 * G * (2 * MOE["H"] * MOE["I"] + MOE["I"] * MOE["H"])
+    return MOE["T"] / (ms * 1e-3), flops / (ms * 1e-3) / 1e12, ms
+
+
+def run_moe(args, tl, synth, dev, world, rank, local):
+    """--workload moe: the C5 layer; on N GPUs expert-parallel (E/N experts and T/N
+    tokens per rank, NCCL all-to-all of the routed rows; strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from ternocl_b200 import dist as tdist
+    m = moe_setup(tl, synth, dev)  # every rank builds the same problem, keeps its share
+    E, topk, T = MOE["E"], MOE["topk"], MOE["T"]
+    if world > 1:
+        EP, Tl = E // world, T // world
+        ex, tok = slice(rank * EP, (rank + 1) * EP), slice(rank * Tl, (rank + 1) * Tl)
+        rows = slice(rank * Tl * topk, (rank + 1) * Tl * topk)
+        layer = tdist.ExpertParallelMoE(E, topk, m["Bg"][ex].contiguous(), m["Sg"][ex].contiguous(),
+                                        m["Bu"][ex].contiguous(), m["Su"][ex].contiguous(), m["Bd"][ex].contiguous(),
+                                        m["Sd"][ex].contiguous())
+        X, ids, RW = m["X"][tok].contiguous(), m["ids"][rows].contiguous(), m["RW"][rows].contiguous()
+        run = lambda: layer(X, ids, RW)
+    else:
+        X = m["X"]
+        run = lambda: moe_layer(tl, m)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        run()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            run()
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # end to end: tokens in from pinned host memory, layer output back every step
+    hX = X.cpu().pin_memory()
+    hO = torch.empty(X.shape, dtype=X.dtype).pin_memory()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        X.copy_(hX, non_blocking=True)
+        O = run()
+        hO.copy_(O if O is not None else m["O"], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    barrier()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    G = T * topk
+    flops = 2.0 * G * (2 * MOE["H"] * MOE["I"] + MOE["I"] * MOE["H"])
+    pk = peaks_tensor()
+    if rank == 0:
+        launches = 7 if world == 1 else 8  # route x2, gather x2, 3 grouped GEMMs, combine
+        line = {"metric": "MoE prefill tokens/s", "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": "int2 MoE prefill layer (configs[4])", **MOE,
+                           "l2": "inputs larger than L2: ~650 MB of weights, routed rows and intermediates",
+                           "parallelism": "expert-parallel x%d, NCCL all-to-all" % world if world > 1 else "single GPU"},
+                "roofline": {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12 / world, "peak": pk[0],
+                             "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / world / pk[0],
+                             "peak_kind": pk[1], "kernel": "gemm_kernel<Int2Gemm, 1> (grouped)", "traffic": None},
+                "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": hX.numel() * 2 * world,
+                        "d2h_bytes_per_step": hO.numel() * 2 * world},
+                "gpu_launches": launches * args.steps, "clocks": clk.summary(),
+                "cpu_baseline": None}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 def run_prefill(args, tl, synth, dev, world, rank, local):
     """--workload prefill: the M=2048 GEMMs as the headline (replicas on N GPUs: weak scaling)."""
     import torch
@@ -291,10 +443,13 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: the headline M=1 GEMV sweep (+ prefill as a secondary figure); "
-                         "prefill: the M=2048 GEMMs alone")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "moe"],
+                    help="decode: the headline M=1 GEMV sweep (+ prefill and MoE as secondary figures); "
+                         "prefill: the M=2048 GEMMs alone; moe: the MoE prefill layer (expert-parallel on N GPUs)")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="capture the K timed steps into one CUDA graph (measured slower than host launches "
+                         "with PDL on B200 for this sequence, so off by default)")
     ap.add_argument("--sets", type=int, default=0,
                     help="weight sets to rotate (default: enough for %.0f GiB)" % WEIGHTS_GIB)
     args = ap.parse_args()
@@ -319,6 +474,8 @@ def main():
     tl.set_option(tl.OPT_PDL, 0 if args.no_pdl else 1)
     if args.workload == "prefill":
         return run_prefill(args, tl, synth, dev, world, rank, local)
+    if args.workload == "moe":
+        return run_moe(args, tl, synth, dev, world, rank, local)
 
     # per-rank column slices (multiples of 16)
     def cols(N):
@@ -355,7 +512,7 @@ def main():
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
 
-    def gemv(ly, s):
+    def gemv(ly, s, sp=sp):
         st = L.ternocl_int2_upcvt(ly["A"].data_ptr(), ly["B"][s].data_ptr(), ly["S"][s].data_ptr(),
                                   ly["C"].data_ptr(), None, None, M, ly["nl"], ly["K"], 0, 0, 0,
                                   tl.ALGO_GEMV, ly["ws"].ptr(), ly["ws"].nbytes(), sp)
@@ -366,7 +523,8 @@ def main():
         s = i % nsets
         for ly in layers:
             gemv(ly, s)
-            if world > 1:
+        if world > 1:
+            for ly in layers:
                 dist.all_gather_into_tensor(ly["Cfull"], ly["C"])
 
     def barrier():
@@ -379,14 +537,34 @@ def main():
         step(i)
     barrier()
 
+    # A decode loop replays captured launches: on one GPU the K timed steps (4 GEMV
+    # launches each, weight set i % nsets) are captured once into a CUDA graph and the
+    # timed region is one replay of it (the C ABI allocates nothing, so its calls capture).
+    timed_graph = None
+    if world == 1 and args.graph:
+        torch.cuda.synchronize()
+        timed_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(timed_graph):
+            cs = torch.cuda.current_stream(dev).cuda_stream
+            for i in range(args.steps):
+                for ly in layers:
+                    gemv(ly, i % nsets, cs)
+
+    def timed_steps():
+        if timed_graph is not None:
+            timed_graph.replay()
+        else:
+            for i in range(args.steps):
+                step(i)
+
+
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
         if args.profile_range:
             torch.cuda.cudart().cudaProfilerStart()
         ev0.record(stream)
-        for i in range(args.steps):
-            step(i)
+        timed_steps()
         ev1.record(stream)
         barrier()
         if args.profile_range:
@@ -403,10 +581,12 @@ def main():
     ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     ev2.record(stream)
-    for i in range(args.steps):
-        s = i % nsets
-        for ly in layers:
-            gemv(ly, s)
+    if timed_graph is not None:
+        timed_graph.replay()
+    else:
+        for i in range(args.steps):
+            for ly in layers:
+                gemv(ly, i % nsets)
     ev3.record(stream)
     barrier()
     kern_ms = ev2.elapsed_time(ev3)
@@ -452,8 +632,14 @@ def main():
     secondary = None
     if world == 1 and not args.no_secondary:
         tf, pms, _ = prefill_measure(tl, synth, dev, steps=min(args.steps, 20), warmup=3)
-        pk = peaks_tensor()
-        secondary = {"prefill": {"metric": "M=2048 int2 fp16 prefill TFLOP/s (tcgen05 GEMM)", "value": tf,
+        pk = pk_moe = peaks_tensor()
+        mt, mtf, mms = moe_measure(tl, synth, dev, steps=min(args.steps, 10), warmup=2)
+        secondary_moe = {"metric": "MoE prefill tokens/s (T=4096, H=2048, I=768, E=128, top-8, fp16)", "value": mt,
+                         "unit": "tokens/s", "ms_per_layer": mms, "tflops": mtf,
+                         "roofline": {"bound": "tensor", "achieved": mtf, "peak": pk_moe[0], "unit": "TFLOP/s",
+                                      "frac": mtf / pk_moe[0], "peak_kind": pk_moe[1]}}
+        secondary = {"moe": secondary_moe,
+                     "prefill": {"metric": "M=2048 int2 fp16 prefill TFLOP/s (tcgen05 GEMM)", "value": tf,
                                  "unit": "TFLOP/s", "ms_per_step": pms, "M": PREFILL_M, "shapes_KxN": SHAPES,
                                  "roofline": {"bound": "tensor", "achieved": tf, "peak": pk[0], "unit": "TFLOP/s",
                                               "frac": tf / pk[0], "peak_kind": pk[1]}}}
@@ -469,7 +655,8 @@ def main():
                        "weights_gib": round(nsets * full_set_bytes / 2 ** 30, 3),
                        "l2": "inputs larger than L2: %d rotating weight sets" % nsets,
                        "parallelism": "N-sharded columns x%d + NCCL all-gather" % world if world > 1 else "single GPU",
-                       "pdl": not args.no_pdl},
+                       "pdl": not args.no_pdl,
+                       "launch": "one CUDA graph of the K timed steps" if (args.graph and world == 1) else "host calls, PDL"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "kernel": "int2_gemv_kernel", "launches": launches,
@@ -484,6 +671,7 @@ def main():
         if secondary:
             line["secondary"] = secondary
         print(json.dumps(line), flush=True)
+    timed_graph = None
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

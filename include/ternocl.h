@@ -81,8 +81,19 @@ int ternocl_device_error(int reset);
  *  TERNOCL_OPT_GEMM_TILE_M (default 0 = chosen per shape): rows of a prefill GEMM
  *    CTA tile, 128 or 256 (no counterpart in the reference, whose tiles are -D
  *    options of its kernels).
+ *  TERNOCL_OPT_GEMV_SPLIT (default 0 = planned per shape): number of CTAs that split
+ *    K in the decode GEMVs, 1..64 (clamped to K/128; above 8 it needs a workspace),
+ *    the counterpart of the reference's LS tile option.
+ *  TERNOCL_OPT_GEMV_WARPS (default 0 = planned per shape): warps per CTA of the int2
+ *    decode GEMV (4, 8 or 16), which split the CTA's K range (the reference's SGM/LS
+ *    tile options have the same role).
  * Returns the previous value, or -1 for an unknown option or value. */
-typedef enum { TERNOCL_OPT_PDL = 1, TERNOCL_OPT_GEMM_TILE_M = 2 } ternocl_option;
+typedef enum {
+    TERNOCL_OPT_PDL = 1,
+    TERNOCL_OPT_GEMM_TILE_M = 2,
+    TERNOCL_OPT_GEMV_SPLIT = 3,
+    TERNOCL_OPT_GEMV_WARPS = 4
+} ternocl_option;
 int ternocl_set_option(int option, int value);
 
 /* Workspace (device scratch) a call may use for its cross-CTA split-K partial sums

@@ -14,6 +14,8 @@ POSTOP_NONE, POSTOP_SILU_MUL, POSTOP_ADD, POSTOP_BIAS, POSTOP_SIGMOID = range(5)
 ALGO_AUTO, ALGO_GEMV, ALGO_GEMM, ALGO_GEMV_TMEM = 0, 1, 2, 3
 OPT_PDL = 1
 OPT_GEMM_TILE_M = 2
+OPT_GEMV_SPLIT = 3
+OPT_GEMV_WARPS = 4
 
 
 def _torch():

@@ -46,6 +46,7 @@ static bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 // GEMV split-K plan: enough CTAs (4 per SM) to keep every SM streaming.
 struct GemvPlan {
     int SK = 1;
+    int warps = 4;         // warps per CTA (register-decode GEMVs)
     bool cluster = false;  // 1 < SK <= 8: reduce through distributed shared memory
     size_t cnt_bytes = 0, part_bytes = 0;
     size_t total() const { return (SK > 1 && !cluster) ? cnt_bytes + part_bytes : 0; }
@@ -70,8 +71,9 @@ static GemvPlan gemv_plan_t(int M, int N, int K, int cols, int rows, int per_sm,
     const long long tiles = (long long)strips * zb;
     const long long target = (long long)per_sm * sm_count();
     int sk = (int)((target + tiles - 1) / tiles);
+    if (options().gemv_split) sk = options().gemv_split;
     if (sk > G) sk = G;
-    if (sk > 32) sk = 32;
+    if (sk > 64) sk = 64;
     while (sk < G && smem_of_sk(sk) > smem_budget) ++sk;
     if (sk > max_cluster && !allow_ws) sk = max_cluster;
     if (sk < 1) sk = 1;
@@ -82,10 +84,33 @@ static GemvPlan gemv_plan_t(int M, int N, int K, int cols, int rows, int per_sm,
     return p;
 }
 
-// warp-level mma.sync GEMV (gemv_int2.cu): 32 columns x 8 rows per CTA
+// warp-level mma.sync GEMV (gemv_int2.cu): 32 columns x 8 rows per CTA of 4, 8 or 16
+// warps
+//
+// Launch shape, searched on B200 over the back-to-back Llama-3-8B decode sequence with
+// PDL (M=1): splitting K across CTAs pays only while there are fewer column strips than
+// SMs (the cross-CTA reduction costs more than the parallelism otherwise); inside a CTA
+// 16 warps split K while the CTA streams <= 32 groups, 8 beyond that, and 4 once the
+// grid already holds >= 4 CTAs per SM (occupancy then matters more).
 static GemvPlan gemv_plan(int M, int N, int K, bool allow_ws) {
-    return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
-                       [&](int sk) { return int2_gemv_smem(M, K, sk); });
+    const int G = K / kGS, sms = sm_count();
+    const long long tiles = (long long)((N + 31) / 32) * ((M + 7) / 8);
+    int sk = options().gemv_split ? options().gemv_split : (tiles < sms ? 2 : 1);
+    if (sk > G) sk = G;
+    int warps = options().gemv_warps;
+    if (!warps) {
+        const int per_cta = (G + sk - 1) / sk;
+        warps = tiles >= 4LL * sms ? 4 : per_cta <= 32 ? 16 : 8;
+    }
+    GemvPlan p;
+    p.SK = sk;
+    while (p.SK < G && int2_gemv_smem(M, K, p.SK, warps) > kGemvSmemBudget) ++p.SK;
+    if (p.SK > kMaxClusterSK && !allow_ws) p.SK = kMaxClusterSK;
+    p.cluster = p.SK > 1 && p.SK <= kMaxClusterSK;
+    p.cnt_bytes = round_up((size_t)tiles * sizeof(unsigned), 256);
+    p.part_bytes = (size_t)p.SK * M * N * sizeof(float);
+    p.warps = warps;
+    return p;
 }
 
 // int1 GEMV (gemv_int1.cu): same CTA shape
@@ -164,6 +189,18 @@ int ternocl_set_option(int option, int value) {
         options().pdl = value ? 1 : 0;
         return old;
     }
+    if (option == TERNOCL_OPT_GEMV_WARPS) {
+        if (value != 0 && value != 4 && value != 8 && value != 16) return -1;
+        const int old = options().gemv_warps;
+        options().gemv_warps = value;
+        return old;
+    }
+    if (option == TERNOCL_OPT_GEMV_SPLIT) {
+        if (value < 0 || value > 64) return -1;
+        const int old = options().gemv_split;
+        options().gemv_split = value;
+        return old;
+    }
     if (option == TERNOCL_OPT_GEMM_TILE_M) {
         if (value != 0 && value != 128 && value != 256) return -1;
         const int old = options().gemm_tile_m;
@@ -191,6 +228,8 @@ int ternocl_device_error(int reset) {
     v |= t;
     if (read_device_error_moe(&t, reset) != cudaSuccess) return -1;
     v |= t;
+    if (read_device_error_gemm_i8(&t, reset) != cudaSuccess) return -1;
+    v |= t;
     return (int)v;
 }
 
@@ -210,9 +249,10 @@ int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
     const bool simt = algo != TERNOCL_ALGO_GEMV_TMEM;
     GemvPlan p = simt ? gemv_plan(M, N, K, ws != nullptr) : gemv_tc_plan(M, N, K, ws != nullptr);
     if (p.total() > ws_bytes) p = simt ? gemv_plan(M, N, K, false) : gemv_tc_plan(M, N, K, false);
-    const size_t smem = simt ? int2_gemv_smem(M, K, p.SK) : int2_gemv_tc_smem(M, K, p.SK);
+    const size_t smem = simt ? int2_gemv_smem(M, K, p.SK, p.warps) : int2_gemv_tc_smem(M, K, p.SK);
     if (smem > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
     a.SK = p.SK;
+    a.warps = p.warps;
     a.cluster = p.cluster ? 1 : 0;
     if (p.total() > 0) {
         if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
@@ -302,13 +342,17 @@ int ternocl_int2_int8(const void *A, const int8_t *Aq, const void *SA, const uin
     int st = check_gemm_common(act, B, SB, C, Other, Bias, M, N, K, dtype, postop, out_f32);
     if (st != TERNOCL_OK) return st;
     if (!SA || !aligned(SA, 2)) return TERNOCL_ERR_ARG;
-    if (algo != TERNOCL_ALGO_AUTO && algo != TERNOCL_ALGO_GEMV) return TERNOCL_ERR_ARG;
+    if (algo != TERNOCL_ALGO_AUTO && algo != TERNOCL_ALGO_GEMV && algo != TERNOCL_ALGO_GEMM) return TERNOCL_ERR_ARG;
     if (M == 0) return TERNOCL_OK;
     GemvArgs a;
     a.A = A; a.B = B; a.S = SB; a.C = C; a.Other = Other; a.Bias = Bias;
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.Aq = Aq; a.SA = SA; a.qmode = qmode;
     a.stream = (cudaStream_t)stream;
+    // the tensor-core GEMM reads the int8 codes (qmode 0); qmode 1 quantises inside the
+    // GEMV kernel, which also serves any M in 8-row blocks
+    if (qmode == 0 && (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM)))
+        return cuda_status(int8_gemm_tc_launch(a));
     // no workspace in this signature: split-K stays within one thread-block cluster
     const GemvPlan p = gemv_i8_plan(M, N, K, false);
     if (int8_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;

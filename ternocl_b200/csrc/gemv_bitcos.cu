@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
     v[0] = acc[0][0]; v[1] = acc[0][2]; v[2] = acc[1][0]; v[3] = acc[1][2];
     v[4] = acc[0][1]; v[5] = acc[0][3]; v[6] = acc[1][1]; v[7] = acc[1][3];
     __syncthreads();  // the table and staging area are reused for the reduction
-    gemv::finish<BitcosCols, DT, POSTOP, OUT_F32>(p, smem, v, colok);
+    gemv::finish<BitcosCols, gemv::kWarps, DT, POSTOP, OUT_F32>(p, smem, v, colok);
 }
 
 template <class DT, int POSTOP, bool OUT_F32>

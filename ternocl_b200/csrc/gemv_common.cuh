@@ -30,9 +30,15 @@
 namespace ternocl {
 namespace gemv {
 
+// CTA size: W warps (4, 8 or 16) split the CTA's K range; kWarps/kThreads are the
+// default (and the BITCOS kernel's) size
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 4;
+constexpr int kMaxWarps = 16;
+#ifndef TERNOCL_GEMV_STAGES
+#define TERNOCL_GEMV_STAGES 4
+#endif
+constexpr int kStages = TERNOCL_GEMV_STAGES;  // cp.async ring depth (groups per warp)
 
 struct Params {
     const uint16_t *A;
@@ -123,8 +129,9 @@ __device__ __forceinline__ void cp_async_wait() {
 // 8-byte scale chunk, laid out [chunk][thread] so a warp's accesses are contiguous.
 // Policy::read_words hands compute() its kWordRegs 16-byte registers from a stage:
 // its own chunks, or (kSharedSlots) chunks copied by other lanes of its warp.
-template <class Policy>
+template <class Policy, int W>
 struct Ring {
+    static constexpr int kThreads = W * 32;
     static constexpr int kStageBytes = (Policy::kWords16 * 16 + 8) * kThreads;
     static constexpr int kBytes = kStages * kStageBytes;
     __device__ static uint4 *words(char *base, int stage, int c, int tid) {
@@ -142,14 +149,21 @@ __host__ __device__ inline int act_row_bytes(int krange) {
     return krange * Policy::kActBytesPerK + Policy::kActPadBytes;
 }
 
-// Bytes of dynamic shared memory for a CTA that stages `krange` K elements of
-// `rows` (<= 8) activation rows.
-template <class Policy>
+// Bytes of dynamic shared memory for a CTA of W warps that stages `krange` K
+// elements of `rows` (<= 8) activation rows.
+template <class Policy, int W>
 __host__ __device__ inline size_t smem_bytes(int rows, int krange) {
     const size_t act = (size_t)rows * act_row_bytes<Policy>(krange);
-    const size_t red = (size_t)kWarps * 32 * 8 * sizeof(float);  // warp partials + CTA partial
-    const size_t ring = Ring<Policy>::kBytes;
+    const size_t red = (size_t)W * 32 * 8 * sizeof(float);  // warp partials + CTA partial
+    const size_t ring = Ring<Policy, W>::kBytes;
     return (ring > red ? ring : red) + act + Policy::extra_smem(rows, krange);
+}
+
+// smem_bytes for a runtime warp count
+template <class Policy>
+inline size_t smem_bytes_w(int warps, int rows, int krange) {
+    return warps >= 16 ? smem_bytes<Policy, 16>(rows, krange)
+                       : warps >= 8 ? smem_bytes<Policy, 8>(rows, krange) : smem_bytes<Policy, 4>(rows, krange);
 }
 
 // Reduction over the CTA's K-split warps (in warp order, through `smem`, >= 8 KB),
@@ -157,7 +171,7 @@ __host__ __device__ inline size_t smem_bytes(int rows, int krange) {
 // and the epilogue store.  v[h*4 + i] = this thread's partial for activation row
 // mb+2q+h and column n0 + ColMap::thread_col(g, i).  Callers synchronise the CTA
 // before reusing `smem`.
-template <class ColMap, class DT, int POSTOP, bool OUT_F32>
+template <class ColMap, int W, class DT, int POSTOP, bool OUT_F32>
 __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], bool colok) {
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -165,7 +179,7 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
     const int n0 = blockIdx.x * 32;
     const int mb = blockIdx.z * 8;
     const int sk = blockIdx.y;
-    float(*red)[32][8] = reinterpret_cast<float(*)[32][8]>(smem);  // [kWarps][lane][8]
+    float(*red)[32][8] = reinterpret_cast<float(*)[32][8]>(smem);  // [W][lane][8]
     if (warp > 0) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) red[warp - 1][lane][i] = v[i];
@@ -173,7 +187,7 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
     __syncthreads();
     if (warp == 0) {
 #pragma unroll
-        for (int w = 0; w < kWarps - 1; ++w)
+        for (int w = 0; w < W - 1; ++w)
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] += red[w][lane][i];
     }
@@ -206,7 +220,7 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
     if (p.cluster) {
         // split-K across the CTAs of a cluster: partials through distributed shared
         // memory, summed by cluster rank 0 in rank (= K split) order
-        float *mine = &red[kWarps - 1][lane][0];
+        float *mine = &red[W - 1][lane][0];
         if (warp == 0) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) mine[i] = v[i];
@@ -262,8 +276,9 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
     if (lane == 0) p.ws_cnt[tile] = 0u;  // ready for the next call
 }
 
-template <class Policy, class DT, int POSTOP, bool OUT_F32>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
+template <class Policy, int W, class DT, int POSTOP, bool OUT_F32>
+__global__ void __launch_bounds__(W * 32) gemv_kernel(const Params p) {
+    using R = Ring<Policy, W>;
     extern __shared__ __align__(128) char smem[];
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -274,13 +289,13 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
     const int sk = blockIdx.y;
     const int cg0 = (int)((long long)G * sk / p.SK), cg1 = (int)((long long)G * (sk + 1) / p.SK);
     const int ng = cg1 - cg0;
-    const int wg0 = cg0 + ng * warp / kWarps, wg1 = cg0 + ng * (warp + 1) / kWarps;
+    const int wg0 = cg0 + ng * warp / W, wg1 = cg0 + ng * (warp + 1) / W;
     const int rows = min(8, p.M - mb);
     const int krange = ng * kGS;
     const bool colok = n0 + Policy::thread_col0(g) < p.N;  // N % 16 == 0
 
     char *ring = smem;
-    char *act = smem + (Ring<Policy>::kBytes > kWarps * 32 * 8 * 4 ? Ring<Policy>::kBytes : kWarps * 32 * 8 * 4);
+    char *act = smem + (R::kBytes > W * 32 * 8 * 4 ? R::kBytes : W * 32 * 8 * 4);
     const int act_stride = act_row_bytes<Policy>(krange);
     char *extra = act + (size_t)rows * act_stride;
 
@@ -297,9 +312,9 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
             if (copyok) {
 #pragma unroll
                 for (int c = 0; c < Policy::kWords16; ++c)
-                    cp_async16(Ring<Policy>::words(ring, stage, c, tid), wsrc + c * cstride);
+                    cp_async16(R::words(ring, stage, c, tid), wsrc + c * cstride);
             }
-            if (colok) cp_async8(Ring<Policy>::scale(ring, stage, tid), ssrc);
+            if (colok) cp_async8(R::scale(ring, stage, tid), ssrc);
         }
         cp_async_commit();
         wsrc += wstride;
@@ -330,8 +345,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
         if (Policy::kSharedSlots) __syncwarp();
         const int stage = i & (kStages - 1);
         uint4 w[Policy::kWordRegs];
-        Policy::read_words(ring + stage * Ring<Policy>::kStageBytes, tid, w);
-        const uint2 sc = *Ring<Policy>::scale(ring, stage, tid);
+        Policy::read_words(ring + stage * R::kStageBytes, tid, W * 32, w);
+        const uint2 sc = *R::scale(ring, stage, tid);
         Policy::template compute<DT>(w, sc, arow, rowok, q, xg, acc, g);
         arow += Policy::kActGroupBytes;
         xg += Policy::kExtraGroupBytes;
@@ -343,7 +358,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
     float v[8];
     Policy::thread_values(acc, v);  // v[h*4 + i]: activation row mb+2q+h, column col(i)
     __syncthreads();  // the ring is reused for the reduction
-    finish<Policy, DT, POSTOP, OUT_F32>(p, smem, v, colok);
+    finish<Policy, W, DT, POSTOP, OUT_F32>(p, smem, v, colok);
 }
 
 }  // namespace gemv

@@ -61,7 +61,7 @@ struct Int1Policy {
     __device__ static size_t chunk_stride(const gemv::Params &) { return 0; }
     __host__ __device__ static size_t extra_smem(int, int) { return 0; }
 
-    __device__ static void read_words(const char *stage, int tid, uint4 *w) {
+    __device__ static void read_words(const char *stage, int tid, int, uint4 *w) {
         const int lane = tid & 31, g = lane >> 2, q = lane & 3;
         const uint4 *base = reinterpret_cast<const uint4 *>(stage) + (tid & ~31) + (g >> 2) * 4 + q;
 #pragma unroll
@@ -73,7 +73,7 @@ struct Int1Policy {
     __device__ static void stage(const gemv::Params &p, char *act, int stride, char *, int mb, int rows, int cg0,
                                  int ng) {
         const int nc = ng * (kGS / 8);  // 16-byte chunks per row
-        for (int it = threadIdx.x; it < rows * nc; it += gemv::kThreads) {
+        for (int it = threadIdx.x; it < rows * nc; it += blockDim.x) {
             const int m = it / nc, c = it - m * nc;
             const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p.A + (size_t)(mb + m) * p.K + (size_t)cg0 * kGS) + c);
             *reinterpret_cast<uint4 *>(act + (size_t)m * stride + (size_t)c * 16) = v;
@@ -133,8 +133,8 @@ cudaError_t launch_t(const GemvArgs &a) {
     const int G = a.K / kGS;
     const int max_ng = (G + a.SK - 1) / a.SK;
     const int rows = a.M < 8 ? a.M : 8;
-    const size_t smem = gemv::smem_bytes<Int1Policy>(rows, max_ng * kGS);
-    auto kern = gemv::gemv_kernel<Int1Policy, DT, POSTOP, OUT_F32>;
+    const size_t smem = gemv::smem_bytes<Int1Policy, gemv::kWarps>(rows, max_ng * kGS);
+    auto kern = gemv::gemv_kernel<Int1Policy, gemv::kWarps, DT, POSTOP, OUT_F32>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -149,7 +149,7 @@ cudaError_t launch_t(const GemvArgs &a) {
 size_t int1_gemv_smem(int M, int K, int SK) {
     const int G = K / kGS;
     const int max_ng = (G + SK - 1) / SK;
-    return gemv::smem_bytes<Int1Policy>(M < 8 ? M : 8, max_ng * kGS);
+    return gemv::smem_bytes<Int1Policy, gemv::kWarps>(M < 8 ? M : 8, max_ng * kGS);
 }
 
 cudaError_t int1_gemv_launch(const GemvArgs &a) {

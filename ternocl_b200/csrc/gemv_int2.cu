@@ -63,9 +63,9 @@ struct Int2Policy {
     static constexpr int kWords16 = 2;
     static constexpr int kWordRegs = kWords16;
     static constexpr bool kSharedSlots = false;
-    __device__ static void read_words(const char *stage, int tid, uint4 *w) {
+    __device__ static void read_words(const char *stage, int tid, int nthreads, uint4 *w) {
 #pragma unroll
-        for (int c = 0; c < kWords16; ++c) w[c] = reinterpret_cast<const uint4 *>(stage)[c * gemv::kThreads + tid];
+        for (int c = 0; c < kWords16; ++c) w[c] = reinterpret_cast<const uint4 *>(stage)[c * nthreads + tid];
     }
     static constexpr bool kContiguousCols = true;
     static constexpr int kActGroupBytes = 8 * 32;   // 8 words x 8 slot registers
@@ -88,7 +88,7 @@ struct Int2Policy {
     __device__ static void stage(const gemv::Params &p, char *act, int stride, char *, int mb, int rows, int cg0,
                                  int ng) {
         const int nw = ng * 8;
-        for (int it = threadIdx.x; it < rows * nw; it += gemv::kThreads) {
+        for (int it = threadIdx.x; it < rows * nw; it += blockDim.x) {
             const int m = it / nw, w = it - m * nw;
             const uint16_t *src = p.A + (size_t)(mb + m) * p.K + (size_t)(cg0 * 8 + w) * 16;
             const uint4 lo = __ldg(reinterpret_cast<const uint4 *>(src));
@@ -158,29 +158,35 @@ struct Int2Policy {
     }
 };
 
-template <class DT, int POSTOP, bool OUT_F32>
-cudaError_t launch_t(const GemvArgs &a) {
+template <int W, class DT, int POSTOP, bool OUT_F32>
+cudaError_t launch_w(const GemvArgs &a) {
     gemv::Params p = gemv::gemv_params_impl(a);
     const int G = a.K / kGS;
     const int max_ng = (G + a.SK - 1) / a.SK;
     const int rows = a.M < 8 ? a.M : 8;
-    const size_t smem = gemv::smem_bytes<Int2Policy>(rows, max_ng * kGS);
-    auto kern = gemv::gemv_kernel<Int2Policy, DT, POSTOP, OUT_F32>;
+    const size_t smem = gemv::smem_bytes<Int2Policy, W>(rows, max_ng * kGS);
+    auto kern = gemv::gemv_kernel<Int2Policy, W, DT, POSTOP, OUT_F32>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
     dim3 grid((a.N + 31) / 32, a.SK, (a.M + 7) / 8);
-    return launch_kernel_cluster(kern, grid, dim3(gemv::kThreads), smem, a.stream,
-                                 dim3(1, a.cluster ? a.SK : 1, 1), p);
+    return launch_kernel_cluster(kern, grid, dim3(W * 32), smem, a.stream, dim3(1, a.cluster ? a.SK : 1, 1), p);
+}
+
+template <class DT, int POSTOP, bool OUT_F32>
+cudaError_t launch_t(const GemvArgs &a) {
+    if (a.warps >= 16) return launch_w<16, DT, POSTOP, OUT_F32>(a);
+    if (a.warps >= 8) return launch_w<8, DT, POSTOP, OUT_F32>(a);
+    return launch_w<4, DT, POSTOP, OUT_F32>(a);
 }
 
 }  // namespace
 
-size_t int2_gemv_smem(int M, int K, int SK) {
+size_t int2_gemv_smem(int M, int K, int SK, int warps) {
     const int G = K / kGS;
     const int max_ng = (G + SK - 1) / SK;
-    return gemv::smem_bytes<Int2Policy>(M < 8 ? M : 8, max_ng * kGS);
+    return gemv::smem_bytes_w<Int2Policy>(warps, M < 8 ? M : 8, max_ng * kGS);
 }
 
 cudaError_t int2_gemv_launch(const GemvArgs &a) {

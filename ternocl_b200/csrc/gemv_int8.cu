@@ -58,9 +58,9 @@ struct Int8Policy {
     static constexpr int kWords16 = 2;
     static constexpr int kWordRegs = kWords16;
     static constexpr bool kSharedSlots = false;
-    __device__ static void read_words(const char *stage, int tid, uint4 *w) {
+    __device__ static void read_words(const char *stage, int tid, int nthreads, uint4 *w) {
 #pragma unroll
-        for (int c = 0; c < kWords16; ++c) w[c] = reinterpret_cast<const uint4 *>(stage)[c * gemv::kThreads + tid];
+        for (int c = 0; c < kWords16; ++c) w[c] = reinterpret_cast<const uint4 *>(stage)[c * nthreads + tid];
     }
     static constexpr bool kContiguousCols = true;
     static constexpr int kActGroupBytes = 8 * 16;   // 8 words x 16 int8
@@ -81,7 +81,7 @@ struct Int8Policy {
     __device__ static void stage(const gemv::Params &p, char *act, int stride, char *extra, int mb, int rows,
                                  int cg0, int ng) {
         const int nw = ng * 8;
-        for (int it = threadIdx.x; it < rows * nw; it += gemv::kThreads) {
+        for (int it = threadIdx.x; it < rows * nw; it += blockDim.x) {
             const int m = it / nw, w = it - m * nw;
             const int grp = cg0 + w / 8;
             const size_t k0 = (size_t)(cg0 * 8 + w) * 16;
@@ -114,7 +114,7 @@ struct Int8Policy {
             *reinterpret_cast<uint4 *>(act + (size_t)m * stride + (size_t)w * 16) = make_uint4(o[0], o[1], o[2], o[3]);
         }
         float *inv = reinterpret_cast<float *>(extra);
-        for (int it = threadIdx.x; it < ng * 8; it += gemv::kThreads) {
+        for (int it = threadIdx.x; it < ng * 8; it += blockDim.x) {
             const int g = it >> 3, m = it & 7;
             float v = 0.0f;
             if (m < rows) {
@@ -176,8 +176,8 @@ cudaError_t launch_t(const GemvArgs &a) {
     const int G = a.K / kGS;
     const int max_ng = (G + a.SK - 1) / a.SK;
     const int rows = a.M < 8 ? a.M : 8;
-    const size_t smem = gemv::smem_bytes<Int8Policy>(rows, max_ng * kGS);
-    auto kern = gemv::gemv_kernel<Int8Policy, DT, POSTOP, OUT_F32>;
+    const size_t smem = gemv::smem_bytes<Int8Policy, gemv::kWarps>(rows, max_ng * kGS);
+    auto kern = gemv::gemv_kernel<Int8Policy, gemv::kWarps, DT, POSTOP, OUT_F32>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -192,7 +192,7 @@ cudaError_t launch_t(const GemvArgs &a) {
 size_t int8_gemv_smem(int M, int K, int SK) {
     const int G = K / kGS;
     const int max_ng = (G + SK - 1) / SK;
-    return gemv::smem_bytes<Int8Policy>(M < 8 ? M : 8, max_ng * kGS);
+    return gemv::smem_bytes<Int8Policy, gemv::kWarps>(M < 8 ? M : 8, max_ng * kGS);
 }
 
 cudaError_t int8_gemv_launch(const GemvArgs &a) {

@@ -17,6 +17,8 @@ struct BF16;
 struct Options {
     int pdl = 0;          // launch with programmatic stream serialization
     int gemm_tile_m = 0;  // prefill GEMM CTA rows: 0 = per shape, 128 or 256
+    int gemv_split = 0;   // decode GEMV K split: 0 = planned per shape
+    int gemv_warps = 0;   // decode GEMV warps per CTA: 0 = planned per shape
 };
 Options &options();
 
@@ -31,6 +33,7 @@ struct GemvArgs {
     int M = 0, N = 0, K = 0;
     int dtype = 0, postop = 0, out_f32 = 0;
     int SK = 1;                  // cross-CTA K split
+    int warps = 4;               // warps per CTA splitting the CTA's K range (4, 8, 16)
     int cluster = 0;             // SK CTAs per thread-block cluster (DSMEM reduction)
     float *ws_part = nullptr;    // [SK][M][N] fp32 partials
     unsigned *ws_cnt = nullptr;  // per-tile arrival counters
@@ -117,7 +120,7 @@ size_t bitcos_gemv_smem(int M, int K, int SK);
 size_t int1_gemv_smem(int M, int K, int SK);
 size_t int8_gemv_smem(int M, int K, int SK);
 cudaError_t int2_gemv_launch(const GemvArgs &a);
-size_t int2_gemv_smem(int M, int K, int SK);
+size_t int2_gemv_smem(int M, int K, int SK, int warps = 4);
 // tcgen05 / TMEM decode GEMV (gemv_tc.cu): 128 columns and tc_gemv_rows(M) rows per CTA
 int tc_gemv_rows(int M);
 size_t int2_gemv_tc_smem(int M, int K, int SK);
@@ -127,6 +130,9 @@ cudaError_t read_device_error_gemv_tc(unsigned *out, int reset);
 cudaError_t int2_gemm_tc_launch(const GemvArgs &a);
 cudaError_t int1_gemm_tc_launch(const GemvArgs &a);
 cudaError_t read_device_error_gemm_tc(unsigned *out, int reset);
+// s8 x s2 prefill GEMM (gemm_i8.cu): a.Aq int8 [M, K], a.SA [K/128, ldsa], a.S = SB
+cudaError_t int8_gemm_tc_launch(const GemvArgs &a);
+cudaError_t read_device_error_gemm_i8(unsigned *out, int reset);
 // grouped (MoE) int2 GEMM over the rows of meta's experts; a.M = G rows
 cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E);
 // MoE routing / gather / combine (moe.cu)

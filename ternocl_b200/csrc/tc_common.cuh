@@ -144,6 +144,15 @@ __device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float (&v)[16]) {
         : "r"(taddr));
 }
 
+// 32x32b load of 16 consecutive 32-bit columns as raw bits (integer accumulators)
+__device__ __forceinline__ void tmem_ld_u32x16(uint32_t taddr, uint32_t *v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
 // ---- MMA ---------------------------------------------------------------------------
 // Instruction descriptor, kind::f16 with fp32 accumulate, A and B K-major:
 // [4,6) D format (1 = f32), [7,10) A format, [10,13) B format (0 = f16, 1 = bf16),

@@ -1,0 +1,108 @@
+"""Multi-GPU paths: one process per GPU, torch.distributed (NCCL over NVLink) for the
+collectives, this library's kernels for the compute.
+
+* Column-sharded decode GEMV (``column_shard``, ``sharded_upcvt``): the columns of a
+  weight matrix are independent (B, S, Bias and Other are column-indexed), so rank r
+  keeps columns [n0, n0 + nl) (multiples of 16), computes its slice of C and the slices
+  are all-gathered.
+* Expert-parallel MoE prefill (``ExpertParallelMoE``): rank r owns experts
+  [r E/P, (r+1) E/P) and T/P tokens.  Routed rows are sorted by owning rank (the route
+  kernel with the ranks as "experts"), counts are exchanged, the rows travel with one
+  all-to-all, the owner runs route/gather/grouped GEMMs (up, gate with SiLU-mul, down)
+  on them, the fp32 results travel back with a second all-to-all and the source rank
+  combines them with its gate weights.
+
+The kernel entry points are parameters (default: the CUDA ones of ``ternocl_b200``), so
+the host-side bookkeeping can be exercised with CPU stand-ins under the gloo backend.
+"""
+import torch
+import torch.distributed as dist
+
+
+def column_shard(N, world, rank, align=16):
+    """(n0, nl): rank's contiguous column slice; all but the last are equal multiples of align."""
+    per = (N // world) // align * align
+    n0 = rank * per
+    return n0, (per if rank < world - 1 else N - n0)
+
+
+def sharded_upcvt(A, B_shard, S_shard, N, upcvt=None, group=None, **kw):
+    """C [M, N] = epi(A @ dequant(B, S)) with this rank holding columns column_shard(N, ...)."""
+    if upcvt is None:
+        from . import int2_upcvt as upcvt
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    C = upcvt(A, B_shard, S_shard, **kw)
+    if world == 1:
+        return C
+    M = C.shape[0]
+    widths = [column_shard(N, world, r)[1] for r in range(world)]
+    wmax = max(widths)
+    buf = C if C.shape[1] == wmax else torch.nn.functional.pad(C, (0, wmax - C.shape[1]))
+    parts = [torch.empty(M, wmax, dtype=C.dtype, device=C.device) for _ in range(world)]
+    dist.all_gather(parts, buf.contiguous(), group=group)
+    return torch.cat([p[:, :w] for p, w in zip(parts, widths)], dim=1)
+
+
+class Kernels:
+    """The four MoE kernel entry points (CUDA by default)."""
+
+    def __init__(self, route=None, gather=None, gemm=None, combine=None):
+        from . import moe_combine, moe_gather, moe_gemm, moe_route
+        self.route = route or moe_route
+        self.gather = gather or moe_gather
+        self.gemm = gemm or moe_gemm
+        self.combine = combine or moe_combine
+
+
+class ExpertParallelMoE:
+    """One MoE prefill layer over P ranks.  Weights are this rank's experts:
+    Bg/Bu int32 [E/P, H/16, I], Bd [E/P, I/16, H], scales [E/P, K/128, N]."""
+
+    def __init__(self, num_experts, topk, Bg, Sg, Bu, Su, Bd, Sd, group=None, kernels=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if num_experts % self.world:
+            raise ValueError("experts must split evenly over the ranks")
+        self.E, self.EP, self.topk = num_experts, num_experts // self.world, topk
+        self.Bg, self.Sg, self.Bu, self.Su, self.Bd, self.Sd = Bg, Sg, Bu, Su, Bd, Sd
+        self.k = kernels or Kernels()
+
+    def _a2a(self, x, out_rows, in_rows):
+        out = torch.empty((sum(out_rows),) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        dist.all_to_all_single(out, x.contiguous(), output_split_sizes=out_rows, input_split_sizes=in_rows,
+                               group=self.group)
+        return out
+
+    def __call__(self, X, ids, RW):
+        """X [T_local, H] (fp16/bf16), ids int32 [T_local*topk] (global expert ids, row g =
+        t*topk + j), RW [T_local*topk] gate weights -> O [T_local, H]."""
+        k, topk = self.k, self.topk
+        T = X.shape[0]
+        # 1. routed rows sorted by owning rank
+        dest = torch.div(ids, self.EP, rounding_mode="floor").to(torch.int32)
+        meta_d, perm_d, inv_d = k.route(dest, self.world)
+        meta_h = meta_d[: self.world + 1].tolist()
+        send = [meta_h[r + 1] - meta_h[r] for r in range(self.world)]
+        Xsend = k.gather(X, perm_d, topk)
+        local_ids = (ids.long()[perm_d.long()] - dest.long()[perm_d.long()] * self.EP).to(torch.int32)
+        # 2. counts, then rows and their local expert ids
+        if self.world > 1:
+            sc = torch.tensor(send, dtype=torch.int64, device=X.device)
+            rc = torch.empty_like(sc)
+            dist.all_to_all_single(rc, sc, group=self.group)
+            recv = rc.tolist()
+            Xrecv = self._a2a(Xsend, recv, send)
+            ids_recv = self._a2a(local_ids, recv, send)
+        else:
+            recv, Xrecv, ids_recv = send, Xsend, local_ids
+        # 3. this rank's experts on the received rows
+        meta_e, perm_e, inv_e = k.route(ids_recv, self.EP)
+        Xs = k.gather(Xrecv, perm_e, 1)
+        up = k.gemm(meta_e, Xs, self.Bu, self.Su, self.EP)
+        Hh = k.gemm(meta_e, Xs, self.Bg, self.Sg, self.EP, postop=1, other=up)
+        Y = k.gemm(meta_e, Hh, self.Bd, self.Sd, self.EP, out_f32=True)
+        Yrecv = Y.index_select(0, inv_e.long())  # back to the received order
+        # 4. results to their source rank (destination-sorted order), weighted combine
+        Yback = self._a2a(Yrecv, send, recv) if self.world > 1 else Yrecv
+        return k.combine(Yback, inv_d, RW, T, topk)

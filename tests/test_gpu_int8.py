@@ -10,7 +10,7 @@ import os
 import numpy as np
 import pytest
 
-from helpers import check_output, dev_any, dev_dt, dev_u32, host_dt
+from helpers import F32_REL_TOL, check_output, dev_any, dev_dt, dev_u32, host_dt, rel_err
 from oracle import api as orc
 from ternocl_b200 import synth
 
@@ -164,3 +164,43 @@ def test_argument_errors(cuda, tl):
     assert L.ternocl_int2_int8(p(A), None, p(SA), p(B), p(SB), p(C), None, None, 1, 40, 256, 0, 0, 0, 1, 0,
                                None) == 1
     assert L.ternocl_int8_quant_a(p(A), p(SA), None, 1, 200, 0, None) == 1
+
+
+# ---- the tcgen05 kind::i8 prefill GEMM (qmode 0: quant_a first, as the reference's
+# upfront-quantisation mode; int2_int8_dpas.cl:283-385)
+GEMM_SHAPES = [(64, 128, 128), (100, 256, 272), (128, 1024, 512), (256, 512, 1024), (77, 4096, 256),
+               (300, 1024, 400), (130, 128, 48)]
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("M,K,N", GEMM_SHAPES)
+def test_gemm_parity(cuda, tl, M, K, N, bf16):
+    c = case(900 + M + K + N, M, K, N, bf16)
+    gold = gold_out(c, M, K, N, bf16, 0, False)
+    A = dev_dt(c["A"], bf16)
+    SA, Aq = tl.int8_quant_a(A)
+    out = host_dt(tl.int2_int8(A, dev_u32(c["B"]), dev_dt(c["SB"], bf16), SA, Aq=Aq, qmode=0, algo=tl.ALGO_GEMM))
+    check_output(out, gold, bf16, False, "s8xs2 gemm M=%d K=%d N=%d bf16=%d" % (M, K, N, bf16))
+    assert tl.device_error() == 0
+
+
+@pytest.mark.parametrize("postop,out_f32", [(0, True), (1, False), (2, False), (3, True), (4, False)])
+def test_gemm_epilogues(cuda, tl, postop, out_f32):
+    M, K, N = 192, 512, 512
+    c = case(40 + postop, M, K, N, 0, postop, out_f32)
+    gold = gold_out(c, M, K, N, 0, postop, out_f32)
+    out = run_gemv(tl, c, 0, postop, out_f32, 0)  # AUTO at M >= 64 with qmode 0 -> the GEMM
+    check_output(out, gold, 0, out_f32, "postop=%d out_f32=%d" % (postop, out_f32))
+
+
+def test_gemm_matches_gemv_kernel(cuda, tl):
+    # the same int32 group dots on both paths: outputs agree within fp32 rounding
+    M, K, N = 96, 2048, 384
+    c = case(8, M, K, N, 1)
+    A = dev_dt(c["A"], 1)
+    SA, Aq = tl.int8_quant_a(A)
+    args = (A, dev_u32(c["B"]), dev_dt(c["SB"], 1), SA)
+    g = host_dt(tl.int2_int8(*args, Aq=Aq, qmode=0, algo=tl.ALGO_GEMM, out_f32=True))
+    v = host_dt(tl.int2_int8(*args, Aq=Aq, qmode=0, algo=tl.ALGO_GEMV, out_f32=True))
+    # the int32 dots are equal; only the fp32 order of the group sums differs
+    assert rel_err(g, v) <= F32_REL_TOL

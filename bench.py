@@ -447,6 +447,8 @@ def main():
                     help="decode: the headline M=1 GEMV sweep (+ prefill and MoE as secondary figures); "
                          "prefill: the M=2048 GEMMs alone; moe: the MoE prefill layer (expert-parallel on N GPUs)")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="N>1: GEMV + NCCL all-gather instead of the GEMV with the all-gather fused in its epilogue")
     ap.add_argument("--graph", action="store_true",
                     help="capture the K timed steps into one CUDA graph (measured slower than host launches "
                          "with PDL on B200 for this sequence, so off by default)")
@@ -504,7 +506,7 @@ def main():
         C = torch.empty(M, nl, dtype=torch.float16, device=dev)
         Cfull = torch.empty(world, M, nl, dtype=torch.float16, device=dev) if world > 1 else None
         ws = tl.Workspace(dev, tl.gemv_workspace_size(M, nl, K))
-        layers.append(dict(K=K, N=N, nl=nl, A=A, B=Bs, S=Ss, C=C, Cfull=Cfull, ws=ws))
+        layers.append(dict(K=K, N=N, n0=n0, nl=nl, A=A, B=Bs, S=Ss, C=C, Cfull=Cfull, ws=ws))
     del B0
     torch.cuda.synchronize()
 
@@ -519,8 +521,17 @@ def main():
         if st != 0:
             raise tl.TernoclError("ternocl_int2_upcvt", st)
 
+    fused = None
+    if world > 1 and not args.nccl_gather:
+        from ternocl_b200 import dist as tdist
+        fused = [tdist.FusedAllGatherGemv(M, ly["N"], ly["K"], torch.float16, dev) for ly in layers]
+
     def step(i):
         s = i % nsets
+        if fused is not None:  # each launch leaves the full C on every rank
+            for ly, fg in zip(layers, fused):
+                fg(ly["A"], ly["B"][s], ly["S"][s])
+            return
         for ly in layers:
             gemv(ly, s)
         if world > 1:
@@ -604,6 +615,10 @@ def main():
         s = i % nsets
         for j, ly in enumerate(layers):
             ly["A"].copy_(hA[j], non_blocking=True)
+            if fused is not None:
+                out = fused[j](ly["A"], ly["B"][s], ly["S"][s])
+                hC[j].copy_(out[:, ly["n0"]:ly["n0"] + ly["nl"]], non_blocking=True)
+                continue
             gemv(ly, s)
             if world > 1:
                 dist.all_gather_into_tensor(ly["Cfull"], ly["C"])
@@ -654,7 +669,9 @@ def main():
             "config": {"workload": WORKLOAD, "M": M, "shapes_KxN": SHAPES, "weight_sets": nsets,
                        "weights_gib": round(nsets * full_set_bytes / 2 ** 30, 3),
                        "l2": "inputs larger than L2: %d rotating weight sets" % nsets,
-                       "parallelism": "N-sharded columns x%d + NCCL all-gather" % world if world > 1 else "single GPU",
+                       "parallelism": ("N-sharded columns x%d + %s" % (world, "NCCL all-gather" if args.nccl_gather else
+                                       "all-gather fused into the GEMV epilogue (NVLink peer stores)"))
+                       if world > 1 else "single GPU",
                        "pdl": not args.no_pdl,
                        "launch": "one CUDA graph of the K timed steps" if (args.graph and world == 1) else "host calls, PDL"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -672,6 +689,10 @@ def main():
             line["secondary"] = secondary
         print(json.dumps(line), flush=True)
     timed_graph = None
+    if fused is not None:
+        torch.cuda.synchronize()
+        for fg in fused:
+            fg.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -135,6 +135,34 @@ int ternocl_int2_upcvt_noalloc(const void *A, const uint32_t *B, const void *S, 
                                const void *Other, const void *Bias, int M, int N, int K, int dtype,
                                int postop, int out_f32, void *stream);
 
+/* Column-sharded int2 GEMV with the all-gather fused into the epilogue (no counterpart in
+ * the reference, which runs on one device; it replaces a GEMV per rank followed by an
+ * NCCL all-gather of the outputs).  Rank `rank` of `world` (<= 8) holds the columns
+ * [n0, n0 + nl) of the weights (B [K/16, nl], S [K/128, nl], contiguous shards) and
+ * stores C[:, n0:n0+nl] into every rank's full C_ranks[r] ([M, N], device pointers valid
+ * in this process, e.g. CUDA IPC mappings of the peers' buffers; Other [M, N] and Bias
+ * [N] are full width).  The launch completes only after all ranks' columns have
+ * arrived: the grid's last CTA writes `epoch` into flags_ranks[r][rank] of every rank and
+ * waits until flags_ranks[rank][r] >= epoch for all r (bounded to ~2 s; a timeout sets
+ * bit 2 of ternocl_device_error).  flags start at 0 and `epoch` must increase by one per
+ * call, in the same order on every rank.  A rank must not read a C buffer after it has
+ * launched the next call that writes it (double-buffer C if the output is consumed across
+ * calls).  ws: >= ternocl_gemv_allgather_workspace_size(M, nl, K) bytes, zeroed once,
+ * 256-byte aligned. */
+size_t ternocl_gemv_allgather_workspace_size(int M, int nl, int K);
+/* CUDA IPC helpers to map the peers' C and flag buffers (set-up time, not the hot path;
+ * plain peer mappings, no multicast objects): the 64-byte handle and byte offset of a
+ * device pointer inside its allocation, the mapping of a peer's handle + offset on the
+ * current device (peer access enabled lazily), and its release. */
+int ternocl_ipc_handle(const void *ptr, void *handle64, size_t *offset);
+int ternocl_ipc_open(const void *handle64, size_t offset, void **ptr);
+int ternocl_ipc_close(void *ptr, size_t offset);
+int ternocl_int2_upcvt_allgather(const void *A, const uint32_t *B, const void *S, void *const *C_ranks,
+                                 const void *Other, const void *Bias, int M, int N, int n0, int nl, int K,
+                                 int dtype, int postop, int out_f32, int rank, int world,
+                                 unsigned *const *flags_ranks, unsigned epoch, void *ws, size_t ws_bytes,
+                                 void *stream);
+
 /* ---------------------------------------------------------------------------------
  * int1 (binary) upconvert GEMM/GEMV.  Replaces int1_fp16_upcvt_gemm / _gemm_mt
  * (int1_fp16_upcvt.cl:166-170, 302-306).  B is the device "sel" layout, uint32

@@ -28,6 +28,12 @@ SIGNATURES = {
     "ternocl_gemv_workspace_size": (sz, [i32, i32, i32]),
     "ternocl_int2_upcvt": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]),
     "ternocl_int2_upcvt_noalloc": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
+    "ternocl_gemv_allgather_workspace_size": (sz, [i32, i32, i32]),
+    "ternocl_ipc_handle": (i32, [vp, vp, vp]),
+    "ternocl_ipc_open": (i32, [vp, sz, vp]),
+    "ternocl_ipc_close": (i32, [vp, sz]),
+    "ternocl_int2_upcvt_allgather": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32,
+                                           i32, vp, C.c_uint, vp, sz, vp]),
     "ternocl_int1_upcvt": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]),
     "ternocl_int8_ldsa": (i32, [i32]),
     "ternocl_int8_quant_a": (i32, [vp, vp, vp, i32, i32, i32, vp]),

@@ -157,6 +157,38 @@ static int check_gemm_common(const void *A, const void *B, const void *S, const 
 }
 
 int gemv_split_k(int M, int N, int K) { return gemv_plan(M, N, K, true).SK; }
+
+// The register-decode int2 GEMV of a width-N matrix (or a width-N shard when `peer` carries
+// the column-sharded fields), planned and launched.
+int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,
+                              const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32, void *ws,
+                              size_t ws_bytes, void *stream, const GemvArgs *peer) {
+    // in the sharded mode C is unused (the peers' C are), Other/Bias are full width
+    int st = check_gemm_common(A, B, S, peer ? (const void *)A : C, peer ? nullptr : Other,
+                               peer ? nullptr : Bias, M, N, K, dtype, peer ? 0 : postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
+    if (postop < 0 || postop > 4) return TERNOCL_ERR_ARG;
+    if ((postop == 1 || postop == 2) && !Other) return TERNOCL_ERR_ARG;
+    if (postop == 3 && !Bias) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    GemvArgs a = peer ? *peer : GemvArgs();
+    a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
+    a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.stream = (cudaStream_t)stream;
+    GemvPlan p = gemv_plan(M, N, K, ws != nullptr);
+    if (p.total() > ws_bytes) p = gemv_plan(M, N, K, false);
+    if (int2_gemv_smem(M, K, p.SK, p.warps) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    a.SK = p.SK;
+    a.warps = p.warps;
+    a.cluster = p.cluster ? 1 : 0;
+    if (p.total() > 0) {
+        if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
+        a.ws_cnt = (unsigned *)ws;
+        a.ws_part = (float *)((char *)ws + p.cnt_bytes);
+    }
+    return cuda_status(int2_gemv_launch(a));
+}
 int report_cuda(cudaError_t e) { return cuda_status(e); }
 
 }  // namespace ternocl
@@ -230,6 +262,8 @@ int ternocl_device_error(int reset) {
     v |= t;
     if (read_device_error_gemm_i8(&t, reset) != cudaSuccess) return -1;
     v |= t;
+    if (read_device_error_allgather(&t, reset) != cudaSuccess) return -1;
+    v |= t;
     return (int)v;
 }
 
@@ -246,21 +280,20 @@ int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
     a.stream = (cudaStream_t)stream;
     if (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM))
         return cuda_status(int2_gemm_tc_launch(a));
-    const bool simt = algo != TERNOCL_ALGO_GEMV_TMEM;
-    GemvPlan p = simt ? gemv_plan(M, N, K, ws != nullptr) : gemv_tc_plan(M, N, K, ws != nullptr);
-    if (p.total() > ws_bytes) p = simt ? gemv_plan(M, N, K, false) : gemv_tc_plan(M, N, K, false);
-    const size_t smem = simt ? int2_gemv_smem(M, K, p.SK, p.warps) : int2_gemv_tc_smem(M, K, p.SK);
-    if (smem > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    if (algo != TERNOCL_ALGO_GEMV_TMEM)
+        return plan_and_launch_int2_gemv(A, B, S, C, Other, Bias, M, N, K, dtype, postop, out_f32, ws, ws_bytes,
+                                         stream, nullptr);
+    GemvPlan p = gemv_tc_plan(M, N, K, ws != nullptr);
+    if (p.total() > ws_bytes) p = gemv_tc_plan(M, N, K, false);
+    if (int2_gemv_tc_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
     a.SK = p.SK;
-    a.warps = p.warps;
     a.cluster = p.cluster ? 1 : 0;
     if (p.total() > 0) {
         if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
         a.ws_cnt = (unsigned *)ws;
         a.ws_part = (float *)((char *)ws + p.cnt_bytes);
     }
-    if (!simt) return cuda_status(int2_gemv_tc_launch(a));
-    return cuda_status(int2_gemv_launch(a));
+    return cuda_status(int2_gemv_tc_launch(a));
 }
 
 int ternocl_int1_upcvt(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,

@@ -35,6 +35,7 @@ namespace gemv {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxWarps = 16;
+constexpr int kMaxPeers = 8;  // ranks of a column-sharded GEMV (one NVLink domain)
 #ifndef TERNOCL_GEMV_STAGES
 #define TERNOCL_GEMV_STAGES 4
 #endif
@@ -57,6 +58,15 @@ struct Params {
     const int8_t *Aq;
     const uint16_t *SA;
     int ldsa, qmode;
+    // column-sharded mode (world > 0): this grid computes columns [n_off, n_off + N) of a
+    // C with N_out columns and stores them into every rank's copy C_peer[r]; Other and
+    // Bias are the full-width arrays.  flag_peer[r] = rank r's flags (one per rank).
+    int world, rank, n_off, N_out;
+    unsigned epoch;
+    unsigned *done_cnt;
+    unsigned *err;  // device error word of the launching library (bit 2: a peer wait timed out)
+    void *C_peer[kMaxPeers];
+    unsigned *flag_peer[kMaxPeers];
 };
 
 // Thread-block cluster helpers (distributed shared memory).
@@ -107,6 +117,17 @@ inline Params gemv_params_impl(const GemvArgs &a) {
     p.SA = (const uint16_t *)a.SA;
     p.ldsa = (a.M + 31) & ~31;
     p.qmode = a.qmode;
+    p.world = a.world;
+    p.rank = a.rank;
+    p.n_off = a.n_off;
+    p.N_out = a.N_out;
+    p.epoch = a.epoch;
+    p.done_cnt = a.done_cnt;
+    p.err = a.err;
+    for (int r = 0; r < kMaxPeers; ++r) {
+        p.C_peer[r] = r < a.world ? a.C_peer[r] : nullptr;
+        p.flag_peer[r] = r < a.world ? a.flag_peer[r] : nullptr;
+    }
     return p;
 }
 
@@ -197,6 +218,21 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
     for (int i = 0; i < 4; ++i) cols[i] = n0 + ColMap::thread_col(g, i);
 
     auto store = [&]() {
+        if (p.world > 0) {  // column-sharded: this rank's columns into every rank's C
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int m = mb + 2 * q + h;
+                if (m < p.M) {
+                    for (int r = 0; r < p.world; ++r) {
+                        epi_store2<DT, POSTOP, OUT_F32>(p.C_peer[r], p.Other, p.Bias, p.N_out, m, p.n_off + cols[0],
+                                                        v[4 * h], v[4 * h + 1]);
+                        epi_store2<DT, POSTOP, OUT_F32>(p.C_peer[r], p.Other, p.Bias, p.N_out, m, p.n_off + cols[2],
+                                                        v[4 * h + 2], v[4 * h + 3]);
+                    }
+                }
+            }
+            return;
+        }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int m = mb + 2 * q + h;
@@ -274,6 +310,46 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
         store();
     }
     if (lane == 0) p.ws_cnt[tile] = 0u;  // ready for the next call
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned *ptr, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *ptr) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t gtimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+
+// Column-sharded completion: every CTA counts itself once its peer stores are fenced;
+// the last CTA of the grid writes `epoch` into its slot of every rank's flags and waits
+// until every rank has written `epoch` into this rank's flags, so the launch completes
+// only when the whole of C has arrived.  The wait gives up after ~2 s (error word bit 2).
+__device__ __forceinline__ void peer_complete(const Params &p, unsigned *err) {
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(p.done_cnt, 1u) != total - 1) return;
+    *p.done_cnt = 0u;  // ready for the next launch
+    __threadfence_system();
+    for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_peer[r] + p.rank, p.epoch);
+    const unsigned *mine = p.flag_peer[p.rank];
+    const uint64_t t0 = gtimer_ns();
+    for (int r = 0; r < p.world; ++r) {
+        uint32_t i = 0;
+        while ((int)(ld_acquire_sys(mine + r) - p.epoch) < 0) {
+            if ((++i & 255u) == 0 && gtimer_ns() - t0 > 2000000000ull) {
+                atomicOr(err, 4u);
+                return;
+            }
+        }
+    }
 }
 
 template <class Policy, int W, class DT, int POSTOP, bool OUT_F32>
@@ -359,6 +435,7 @@ __global__ void __launch_bounds__(W * 32) gemv_kernel(const Params p) {
     Policy::thread_values(acc, v);  // v[h*4 + i]: activation row mb+2q+h, column col(i)
     __syncthreads();  // the ring is reused for the reduction
     finish<Policy, W, DT, POSTOP, OUT_F32>(p, smem, v, colok);
+    if (p.world > 0) peer_complete(p, p.err);
 }
 
 }  // namespace gemv

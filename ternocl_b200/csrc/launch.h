@@ -45,6 +45,13 @@ struct GemvArgs {
     // BITCOS: slice ranks [ls-1][N] of the reference's ls K slices
     const uint32_t *SR = nullptr;
     int ls = 1;
+    // column-sharded GEMV (world > 0): see gemv::Params
+    int world = 0, rank = 0, n_off = 0, N_out = 0;
+    unsigned epoch = 0;
+    unsigned *done_cnt = nullptr;
+    unsigned *err = nullptr;
+    void *C_peer[8] = {};
+    unsigned *flag_peer[8] = {};
 };
 
 template <class T>
@@ -149,5 +156,11 @@ constexpr int kGemmMinM = 64;
 int gemv_split_k(int M, int N, int K);
 // CUDA error -> ternocl status (records ternocl_last_error)
 int report_cuda(cudaError_t e);
+// plan + launch of the register-decode int2 GEMV; `peer` (or null) carries the
+// column-sharded fields of ternocl_int2_upcvt_allgather
+int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, void *C, const void *Other,
+                              const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32, void *ws,
+                              size_t ws_bytes, void *stream, const GemvArgs *peer);
+cudaError_t read_device_error_allgather(unsigned *out, int reset);
 
 }  // namespace ternocl

@@ -43,6 +43,84 @@ def sharded_upcvt(A, B_shard, S_shard, N, upcvt=None, group=None, **kw):
     return torch.cat([p[:, :w] for p, w in zip(parts, widths)], dim=1)
 
 
+def ipc_peers(t, group=None):
+    """Every rank's tensor `t` (same shape and dtype on every rank) as device pointers valid
+    in this process: its own, and the peers' mapped by CUDA IPC (plain peer mappings).
+    Returns (pointers, mapped) where mapped lists (pointer, offset) to release later."""
+    import ctypes
+    from ._lib import call
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    h = (ctypes.c_uint8 * 64)()
+    off = ctypes.c_size_t(0)
+    call("ternocl_ipc_handle", t.data_ptr(), ctypes.addressof(h), ctypes.byref(off))
+    mine = torch.tensor(list(bytes(h)) + list(int(off.value).to_bytes(8, "little")), dtype=torch.uint8,
+                        device=t.device)
+    everyone = torch.empty(world, mine.numel(), dtype=torch.uint8, device=t.device)
+    dist.all_gather_into_tensor(everyone, mine, group=group)
+    rows = everyone.cpu().numpy()
+    ptrs, mapped = [], []
+    for r in range(world):
+        if r == rank:
+            ptrs.append(t.data_ptr())
+            continue
+        hh = (ctypes.c_uint8 * 64).from_buffer_copy(rows[r][:64].tobytes())
+        o = int.from_bytes(rows[r][64:72].tobytes(), "little")
+        p = ctypes.c_void_p(0)
+        call("ternocl_ipc_open", ctypes.addressof(hh), o, ctypes.byref(p))
+        ptrs.append(p.value)
+        mapped.append((p.value, o))
+    return ptrs, mapped
+
+
+class FusedAllGatherGemv:
+    """Column-sharded int2 GEMV whose epilogue writes this rank's columns into every
+    rank's C (ternocl_int2_upcvt_allgather): C [M, N] is complete on every rank when the
+    launch finishes, with no separate collective.  Two C buffers alternate between calls
+    so a rank may read the previous output while the next call is being written."""
+
+    def __init__(self, M, N, K, dtype, device, group=None):
+        import ctypes
+        from . import dtype_code, lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.M, self.N, self.K = M, N, K
+        self.n0, self.nl = column_shard(N, self.world, self.rank)
+        self.dt = dtype_code(torch.empty(0, dtype=dtype))
+        self.C = [torch.empty(M, N, dtype=dtype, device=device) for _ in range(2)]
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=device)
+        self.ws = torch.zeros(lib().ternocl_gemv_allgather_workspace_size(M, self.nl, K), dtype=torch.uint8,
+                              device=device)
+        self._mapped = []
+        self.c_ptrs = []
+        for c in self.C:
+            ptrs, mapped = ipc_peers(c, group)
+            self.c_ptrs.append((ctypes.c_void_p * self.world)(*ptrs))
+            self._mapped += mapped
+        fptrs, mapped = ipc_peers(self.flags, group)
+        self.f_ptrs = (ctypes.c_void_p * self.world)(*fptrs)
+        self._mapped += mapped
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def __call__(self, A, B_shard, S_shard, postop=0, other=None, bias=None, stream=None):
+        """A [M, K]; B_shard [K/16, nl], S_shard [K/128, nl] = this rank's columns.  Returns C."""
+        from . import _ptr, _stream, call
+        self.epoch += 1
+        buf = self.epoch & 1
+        call("ternocl_int2_upcvt_allgather", _ptr(A), _ptr(B_shard), _ptr(S_shard), self.c_ptrs[buf], _ptr(other),
+             _ptr(bias), self.M, self.N, self.n0, self.nl, self.K, self.dt, int(postop), 0, self.rank, self.world,
+             self.f_ptrs, self.epoch, self.ws.data_ptr(), self.ws.numel(), _stream(stream))
+        return self.C[buf]
+
+    def close(self):
+        from ._lib import lib
+        for p, o in self._mapped:
+            lib().ternocl_ipc_close(p, o)
+        self._mapped = []
+
+
 class Kernels:
     """The four MoE kernel entry points (CUDA by default)."""
 

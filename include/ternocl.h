@@ -87,12 +87,17 @@ int ternocl_device_error(int reset);
  *  TERNOCL_OPT_GEMV_WARPS (default 0 = planned per shape): warps per CTA of the int2
  *    decode GEMV (4, 8 or 16), which split the CTA's K range (the reference's SGM/LS
  *    tile options have the same role).
+ *  TERNOCL_OPT_GEMM_PERSISTENT (default 0): the persistent tcgen05 GEMM (one CTA per
+ *    SM over all tiles, epilogue overlapped with the next tile) for 0 = no GEMM,
+ *    1 = the MoE grouped GEMMs, 2 = every prefill GEMM (measured slower than one CTA
+ *    per tile on B200 for the shapes benchmarked here).
  * Returns the previous value, or -1 for an unknown option or value. */
 typedef enum {
     TERNOCL_OPT_PDL = 1,
     TERNOCL_OPT_GEMM_TILE_M = 2,
     TERNOCL_OPT_GEMV_SPLIT = 3,
-    TERNOCL_OPT_GEMV_WARPS = 4
+    TERNOCL_OPT_GEMV_WARPS = 4,
+    TERNOCL_OPT_GEMM_PERSISTENT = 5
 } ternocl_option;
 int ternocl_set_option(int option, int value);
 

@@ -16,6 +16,7 @@ OPT_PDL = 1
 OPT_GEMM_TILE_M = 2
 OPT_GEMV_SPLIT = 3
 OPT_GEMV_WARPS = 4
+OPT_GEMM_PERSISTENT = 5
 
 
 def _torch():

@@ -221,6 +221,12 @@ int ternocl_set_option(int option, int value) {
         options().pdl = value ? 1 : 0;
         return old;
     }
+    if (option == TERNOCL_OPT_GEMM_PERSISTENT) {
+        if (value < 0 || value > 2) return -1;
+        const int old = options().gemm_persistent;
+        options().gemm_persistent = value;
+        return old;
+    }
     if (option == TERNOCL_OPT_GEMV_WARPS) {
         if (value != 0 && value != 4 && value != 8 && value != 16) return -1;
         const int old = options().gemv_warps;

@@ -62,8 +62,8 @@ template <int HALVES>
 struct Cfg {
     static constexpr int kRows = BM * HALVES;
     static constexpr int kLoadStages = HALVES == 2 ? 3 : 4;
-    // A (K-major, no swizzle): box c (K = 8c .. 8c+7) = kRows rows x 16 bytes at c * kALBO
-    static constexpr int kALBO = kRows * 16, kASBO = 128;
+    // A (K-major, 128-byte swizzle): one TMA box of kRows rows x 64 elements per stage;
+    // the 128-row half h starts at h * 16 KB
     static constexpr int kAStageBytes = kRows * BK * 2;
     static constexpr int kTmemCols = BN * HALVES;
     // decoded buffers first: every descriptor-derived address stays inside the block
@@ -72,7 +72,7 @@ struct Cfg {
     static constexpr int pack = a + kLoadStages * kAStageBytes;
     static constexpr int scale = pack + kLoadStages * kPackStageBytes;
     static constexpr int bars = scale + kLoadStages * kScaleStageBytes;
-    static constexpr int total = bars + 256;
+    static constexpr int total = bars + 256 + 1024;  // + alignment slack
     static_assert(total <= 227 * 1024, "shared memory");
 };
 
@@ -103,6 +103,16 @@ __device__ __forceinline__ void mma_ss_f16(uint32_t d_tmem, uint64_t a_desc, uin
         "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Shared-memory descriptor of a K-major operand in the 128-byte swizzle layout written by
+// TMA with CU_TENSOR_MAP_SWIZZLE_128B: rows of 64 16-bit elements (128 B), the 16-byte
+// chunks of row r permuted by r % 8, 8-row groups 1024 B apart (SBO), the tile based at a
+// 1024-byte boundary; layout type 2 (SWIZZLE_128B) in bits 61-63, version 1.  A K=16
+// slice of the MMA starts 32 B further into the row.
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
 }
 
 template <class DT>
@@ -187,7 +197,9 @@ template <class Policy, int HALVES, class DT, int POSTOP, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, const __grid_constant__ CUtensorMap tmA) {
     using C = Cfg<HALVES>;
     constexpr int kLoadStages = C::kLoadStages;
-    extern __shared__ __align__(1024) char smem[];
+    extern __shared__ __align__(1024) char smem_raw[];
+    // 1024-byte aligned base (the 128-byte swizzle pattern is anchored at 1024 B)
+    char *smem = smem_raw + ((1024u - (tc::smem_addr(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * BN;
     Params p = pin;
@@ -248,8 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
                 if (kb >= kLoadStages && !tc::mbar_wait(&load_empty[s], ((kb / kLoadStages) - 1) & 1)) break;
                 tc::mbar_expect_tx(&full[s], C::kAStageBytes + pack_bytes + scale_bytes);
                 char *a = smem + C::a + s * C::kAStageBytes;
-#pragma unroll
-                for (int c = 0; c < BK / 8; ++c) tma_load_2d(a + c * C::kALBO, &tmA, kb * BK + 8 * c, m0, &full[s]);
+                tma_load_2d(a, &tmA, kb * BK, m0, &full[s]);
                 char *pk = smem + C::pack + s * kPackStageBytes;
                 for (int r = 0; r < Policy::kRowsPerStage; ++r)
                     tc::bulk_g2s(pk + r * (BN * 4), Policy::row_ptr(p, kb, r, n0), pack_bytes / Policy::kRowsPerStage,
@@ -279,8 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
 #pragma unroll
                     for (int h = 0; h < HALVES; ++h) {
                         // rows 128h .. 128h+127 of the A stage: 16 core matrices from h * 2048
-                        const uint64_t ad = tc::sdesc_kmajor_noswz(a + kk * 2 * C::kALBO + h * BM * 16, C::kALBO,
-                                                                   C::kASBO);
+                        const uint64_t ad = sdesc_kmajor_sw128(a + h * BM * 128 + kk * 32);
                         mma_ss_f16(tmem + h * BN, ad, bd, idesc, (kb | kk) != 0);
                     }
                 }
@@ -338,6 +348,218 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
     }
 }
 
+// ---- persistent variant ---------------------------------------------------------
+// One CTA per SM walks the tiles (column block fastest); 128-row tiles with two TMEM
+// accumulators (2 x 256 columns) so that four dedicated epilogue warps drain tile i
+// while the producer, decode and MMA warps already run tile i+1.  The pipeline's stage
+// and phase counters simply continue across tiles.  Used for the MoE grouped GEMMs
+// (many short tiles) and wherever the per-launch tile count leaves a ragged last wave.
+constexpr int kPEpiWarps = 4;
+constexpr int kPThreads = (2 + kDecWarps + kPEpiWarps) * 32;  // 448
+
+struct TileInfo {
+    int m0, m_end, n0;
+    const uint32_t *B;
+    const uint16_t *S;
+};
+
+// tile t of the launch -> rows, columns and (grouped mode) the expert's weights
+template <class Policy>
+__device__ __forceinline__ bool tile_info(const Params &p, int t, int nN, TileInfo &ti) {
+    const int tm = t / nN, tn = t - tm * nN;
+    ti.n0 = tn * BN;
+    ti.B = p.B;
+    ti.S = p.S;
+    if (!p.meta) {
+        ti.m0 = tm * BM;
+        ti.m_end = p.M;
+        return true;
+    }
+    const int E = p.E;
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.meta[E + 1 + mid] <= tm) lo = mid;
+        else hi = mid - 1;
+    }
+    ti.m0 = p.meta[lo] + (tm - p.meta[E + 1 + lo]) * BM;
+    ti.m_end = p.meta[lo + 1];
+    ti.B = p.B + (size_t)lo * (p.K / Policy::kKPerWordRow) * p.N;
+    ti.S = p.S + (size_t)lo * (p.K / kGS) * p.N;
+    return true;
+}
+
+template <class Policy, class DT, int POSTOP, bool OUT_F32>
+__global__ void __launch_bounds__(kPThreads, 1) gemm_persistent_kernel(const Params p,
+                                                                       const __grid_constant__ CUtensorMap tmA) {
+    using C = Cfg<1>;
+    constexpr int kLoadStages = C::kLoadStages;
+    extern __shared__ __align__(1024) char smem_raw[];
+    // 1024-byte aligned base (the 128-byte swizzle pattern is anchored at 1024 B)
+    char *smem = smem_raw + ((1024u - (tc::smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nk = p.K / BK;
+    const int nN = (p.N + BN - 1) / BN;
+    if (p.meta) pdl_wait();  // the tile count comes from the routing kernel
+    const int ntiles = (p.meta ? p.meta[2 * p.E + 1] : (p.M + BM - 1) / BM) * nN;
+    if ((int)blockIdx.x >= ntiles) return;
+
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::bars);
+    uint64_t *load_empty = full + kLoadStages;
+    uint64_t *dec_full = load_empty + kLoadStages;
+    uint64_t *dec_empty = dec_full + kDecStages;
+    uint64_t *acc_full = dec_empty + kDecStages;  // [2]
+    uint64_t *acc_empty = acc_full + 2;           // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+
+    if (tid == 0) {
+        for (int s = 0; s < kLoadStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&load_empty[s], 1 + kDecWarps);
+        }
+        for (int d = 0; d < kDecStages; ++d) {
+            tc::mbar_init(&dec_full[d], kDecWarps);
+            tc::mbar_init(&dec_empty[d], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&acc_full[b], 1);
+            tc::mbar_init(&acc_empty[b], kPEpiWarps);
+        }
+        tc::fence_mbar_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, 2 * BN);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            if (!p.meta) pdl_wait();
+            int g = 0;  // stages issued so far, across tiles
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                TileInfo ti;
+                tile_info<Policy>(p, t, nN, ti);
+                const int ncols = min(BN, p.N - ti.n0);
+                const uint32_t pack_bytes = Policy::kRowsPerStage * ncols * 4, scale_bytes = ncols * 2;
+                Params q = p;
+                q.B = ti.B;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % kLoadStages;
+                    if (g >= kLoadStages && !tc::mbar_wait(&load_empty[s], ((g / kLoadStages) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_expect_tx(&full[s], C::kAStageBytes + pack_bytes + scale_bytes);
+                    char *a = smem + C::a + s * C::kAStageBytes;
+                    tma_load_2d(a, &tmA, kb * BK, ti.m0, &full[s]);
+                    char *pk = smem + C::pack + s * kPackStageBytes;
+                    for (int r = 0; r < Policy::kRowsPerStage; ++r)
+                        tc::bulk_g2s(pk + r * (BN * 4), Policy::row_ptr(q, kb, r, ti.n0),
+                                     pack_bytes / Policy::kRowsPerStage, &full[s]);
+                    tc::bulk_g2s(smem + C::scale + s * kScaleStageBytes,
+                                 ti.S + (size_t)(kb * BK / kGS) * p.N + ti.n0, scale_bytes, &full[s]);
+                }
+            }
+            for (int x = g - kLoadStages < 0 ? 0 : g - kLoadStages; x < g; ++x)
+                tc::mbar_wait(&full[x % kLoadStages], (x / kLoadStages) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_f16(DT::kBF16, BM, BN) | (1u << 16);
+            int g = 0, it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+                const int b = it & 1;
+                if (it >= 2 && !tc::mbar_wait(&acc_empty[b], ((it >> 1) - 1) & 1)) break;
+                tc::fence_after_sync();
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % kLoadStages, d = g % kDecStages;
+                    if (!tc::mbar_wait(&full[s], (g / kLoadStages) & 1) ||
+                        !tc::mbar_wait(&dec_full[d], (g / kDecStages) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t a = tc::smem_addr(smem + C::a + s * C::kAStageBytes);
+                    const uint32_t bb = tc::smem_addr(smem + C::dec + d * kDecStageBytes);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t bd = tc::sdesc_kmajor_noswz(bb + kk * 2 * kDecLBO, kDecLBO, kDecSBO);
+                        const uint64_t ad = sdesc_kmajor_sw128(a + kk * 32);
+                        mma_ss_f16(tmem + b * BN, ad, bd, idesc, (kb | kk) != 0);
+                    }
+                    tc::mma_commit(&load_empty[s]);
+                    tc::mma_commit(&dec_empty[d]);
+                }
+                if (ok) tc::mma_commit(&acc_full[b]);
+            }
+        }
+    } else if (warp < 2 + kDecWarps) {
+        const int kc = warp - 2, nb = lane;
+        int g = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = g % kLoadStages, d = g % kDecStages;
+                if (!tc::mbar_wait(&full[s], (g / kLoadStages) & 1) ||
+                    (g >= kDecStages && !tc::mbar_wait(&dec_empty[d], ((g / kDecStages) - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                uint4 rows[8];
+                Policy::template decode<DT>(smem + C::pack + s * kPackStageBytes,
+                                            reinterpret_cast<const uint16_t *>(smem + C::scale + s * kScaleStageBytes),
+                                            kc, nb, rows);
+                char *dst = smem + C::dec + d * kDecStageBytes + nb * kDecSBO + kc * 128;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4 *>(dst + r * 16) = rows[r];
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::mbar_arrive(&dec_full[d]);
+                    tc::mbar_arrive(&load_empty[s]);
+                }
+            }
+        }
+    } else {
+        // epilogue: warp w owns TMEM lanes 32(w%4)..+31, all 256 columns of the tile
+        const int quad = warp & 3;
+        int it = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+            const int b = it & 1;
+            if (!tc::mbar_wait(&acc_full[b], (it >> 1) & 1)) break;
+            tc::fence_after_sync();
+            TileInfo ti;
+            tile_info<Policy>(p, t, nN, ti);
+            const int ncols = min(BN, p.N - ti.n0);
+            const int m = ti.m0 + 32 * quad + lane;
+#pragma unroll 1
+            for (int c = 0; c < BN / 16; ++c) {
+                float v[16];
+                tc::tmem_ld<16>(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(b * BN + 16 * c), v);
+                tc::tmem_wait_ld();
+                if (m < ti.m_end && 16 * c < ncols) {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2)
+                        epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, ti.n0 + 16 * c + i, v[i], v[i + 1]);
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+        }
+        pdl_launch_dependents();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -357,19 +579,51 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// A [M, K] DT row-major; boxes of box_rows rows x 8 elements, rows past M read as zero
+// A [M, K] DT row-major; boxes of box_rows rows x 64 elements in the 128-byte swizzle
+// layout, rows past M read as zero
 static cudaError_t make_map_a(CUtensorMap *map, const void *A, int M, int K, bool bf16, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {8, (cuuint32_t)box_rows};
+    const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                           const_cast<void *>(A), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <class Policy>
+cudaError_t launch_persistent(const GemvArgs &a, const int *meta = nullptr, int E = 0) {
+    CUtensorMap map;
+    cudaError_t e = make_map_a(&map, a.A, a.M, a.K, a.dtype == TERNOCL_BF16, BM);
+    if (e != cudaSuccess) return e;
+    Params p;
+    p.meta = meta;
+    p.E = E;
+    p.B = a.B;
+    p.S = (const uint16_t *)a.S;
+    p.C = a.C;
+    p.Other = (const uint16_t *)a.Other;
+    p.Bias = a.Bias;
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // upper bound of the tile count (grouped: every expert adds at most one partial tile);
+    // CTAs beyond the actual count return at once
+    const long long tiles = ((long long)(a.M + BM - 1) / BM + (meta ? E : 0)) * ((a.N + BN - 1) / BN);
+    const int grid = (int)(tiles < sms ? tiles : sms);
+    return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
+        using DT = typename decltype(dt)::type;
+        auto kern = gemm_persistent_kernel<Policy, DT, decltype(po)::value, decltype(of)::value>;
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<1>::total);
+        if (err != cudaSuccess) return err;
+        return launch_kernel(kern, dim3(grid), dim3(kPThreads), (size_t)Cfg<1>::total, a.stream, p, map);
+    });
 }
 
 template <class Policy, int HALVES>
@@ -420,15 +674,18 @@ static bool use_256_rows(int M, int N) {
 }  // namespace gemm
 
 cudaError_t int2_gemm_tc_launch(const GemvArgs &a) {
+    if (options().gemm_persistent == 2) return gemm::launch_persistent<gemm::Int2Gemm>(a);
     return gemm::use_256_rows(a.M, a.N) ? gemm::launch_policy<gemm::Int2Gemm, 2>(a)
                                         : gemm::launch_policy<gemm::Int2Gemm, 1>(a);
 }
 cudaError_t int1_gemm_tc_launch(const GemvArgs &a) {
+    if (options().gemm_persistent == 2) return gemm::launch_persistent<gemm::Int1Gemm>(a);
     return gemm::use_256_rows(a.M, a.N) ? gemm::launch_policy<gemm::Int1Gemm, 2>(a)
                                         : gemm::launch_policy<gemm::Int1Gemm, 1>(a);
 }
 cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E) {
-    return gemm::launch_policy<gemm::Int2Gemm, 1>(a, meta, E);
+    if (options().gemm_persistent == 0) return gemm::launch_policy<gemm::Int2Gemm, 1>(a, meta, E);
+    return gemm::launch_persistent<gemm::Int2Gemm>(a, meta, E);
 }
 cudaError_t read_device_error_gemm_tc(unsigned *out, int reset) { return tc::read_tu_error(out, reset); }
 

@@ -19,6 +19,7 @@ struct Options {
     int gemm_tile_m = 0;  // prefill GEMM CTA rows: 0 = per shape, 128 or 256
     int gemv_split = 0;   // decode GEMV K split: 0 = planned per shape
     int gemv_warps = 0;   // decode GEMV warps per CTA: 0 = planned per shape
+    int gemm_persistent = 0;  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every prefill GEMM
 };
 Options &options();
 

@@ -8,13 +8,13 @@
 //
 // The grouped GEMM itself is the tcgen05 GEMM in grouped mode (gemm_tc.cu).
 //
-// Routing is one CTA, like the reference's single work-group, but the order of the
-// rows inside an expert is ascending in g (the reference's follows its local
-// atomics): counts with shared-memory atomics, then the rows are placed in rounds of
-// 1024; inside a round a row's position is its expert's running offset + the count of
-// the same expert in lower warps (a 32-step scan per expert) + its rank among the
-// lanes of its warp with the same expert (__match_any_sync).  Expert ids outside
-// [0, E) are skipped and flagged in the device error word (bit 1).
+// Routing: the order of the rows inside an expert is ascending in g (the reference's
+// follows its local atomics), so it is deterministic.  Up to 1024 rows one CTA (like
+// the reference's single work-group): counts with shared-memory atomics, then a row's
+// position is its expert's offset + the count of the same expert in lower warps (a
+// 32-step scan per expert) + its rank among the lanes of its warp with the same expert
+// (__match_any_sync); beyond that one CTA per 1024 rows (moe_route_mc_kernel).  Expert
+// ids outside [0, E) are skipped and flagged in the device error word (bit 1).
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -91,6 +91,80 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const int *__r
     pdl_launch_dependents();
 }
 
+// Multi-CTA form of the same routing (same outputs): CTA c places rows
+// [1024c, 1024c + 1024).  Every CTA histograms all ids (the experts' totals -> their row
+// offsets) and the ids before its chunk (its starting offset inside each expert), so no
+// scratch memory is needed; CTA 0 writes meta.  Inside the chunk the placement is the
+// single-CTA kernel's round.
+__global__ void __launch_bounds__(kRouteThreads) moe_route_mc_kernel(const int *__restrict__ ids, int *meta,
+                                                                    int *perm, int *inv, int G, int E, int rpt) {
+    extern __shared__ int sm[];
+    int *tot = sm;          // [E] rows per expert (all G)
+    int *base = sm + E;     // [E] first row of this chunk's rows of expert e
+    int *wc = sm + 2 * E;   // [32][E]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c0 = blockIdx.x * kRouteThreads;
+    pdl_wait();
+    for (int e = tid; e < E; e += kRouteThreads) {
+        tot[e] = 0;
+        base[e] = 0;
+    }
+    for (int i = tid; i < 32 * E; i += kRouteThreads) wc[i] = 0;
+    __syncthreads();
+    bool bad = false;
+    for (int g = tid; g < G; g += kRouteThreads) {
+        const int e = ids[g];
+        if (e >= 0 && e < E) {
+            atomicAdd(&tot[e], 1);
+            if (g < c0) atomicAdd(&base[e], 1);
+        } else {
+            bad = true;
+        }
+    }
+    if (bad && blockIdx.x == 0) atomicOr(&tc::g_device_error, 2u);
+    __syncthreads();
+    if (tid == 0) {
+        int r = 0, t = 0;
+        for (int e = 0; e < E; ++e) {
+            const int c = tot[e];
+            if (blockIdx.x == 0) {
+                meta[e] = r;
+                meta[E + 1 + e] = t;
+            }
+            base[e] += r;
+            r += c;
+            t += (c + rpt - 1) / rpt;
+        }
+        if (blockIdx.x == 0) {
+            meta[E] = r;
+            meta[2 * E + 1] = t;
+        }
+    }
+    __syncthreads();
+    const int g = c0 + tid;
+    int e = g < G ? ids[g] : -1;
+    if (e >= E) e = -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wc[warp * E + e] = __popc(peers);
+    __syncthreads();
+    for (int x = tid; x < E; x += kRouteThreads) {
+        int acc = 0;
+        for (int w = 0; w < 32; ++w) {
+            const int cnt = wc[w * E + x];
+            wc[w * E + x] = acc;
+            acc += cnt;
+        }
+    }
+    __syncthreads();
+    if (e >= 0) {
+        const int pos = base[e] + wc[warp * E + e] + rank;
+        perm[pos] = g;
+        inv[g] = pos;
+    }
+    pdl_launch_dependents();
+}
+
 // one CTA row: Xs[p] = X[perm[p] / topk], 16-byte copies
 __global__ void __launch_bounds__(256) moe_gather_kernel(const uint4 *__restrict__ X, const int *__restrict__ perm,
                                                         uint4 *__restrict__ Xs, int G, int K8, int topk) {
@@ -138,11 +212,13 @@ size_t moe_route_smem(int E) { return (size_t)(2 * E + 32 * E) * sizeof(int); }
 cudaError_t moe_route_launch(const int *ids, int *meta, int *perm, int *inv, int G, int E, int rpt,
                              cudaStream_t st) {
     const size_t smem = moe_route_smem(E);
+    auto kern = G > kRouteThreads ? moe_route_mc_kernel : moe_route_kernel;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_kernel(moe_route_kernel, dim3(1), dim3(kRouteThreads), smem, st, ids, meta, perm, inv, G, E, rpt);
+    const int ctas = G > kRouteThreads ? (G + kRouteThreads - 1) / kRouteThreads : 1;
+    return launch_kernel(kern, dim3(ctas), dim3(kRouteThreads), smem, st, ids, meta, perm, inv, G, E, rpt);
 }
 
 cudaError_t moe_gather_launch(const void *X, const int *perm, void *Xs, int G, int K, int topk, cudaStream_t st) {

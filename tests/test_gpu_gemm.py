@@ -24,9 +24,15 @@ def run_int2(tl, c, bf16, postop, out_f32, algo):
     return host_dt(tl.int2_upcvt(A, B, S, postop=postop, out_f32=out_f32, other=other, bias=bias, algo=algo))
 
 
-@pytest.fixture(params=[0, 128, 256], ids=["tile_auto", "tile128", "tile256"])
+@pytest.fixture(params=[0, 128, 256, "persistent"], ids=["tile_auto", "tile128", "tile256", "persistent"])
 def tile_m(request, tl):
-    """Every prefill test runs with the per-shape tile choice and with each tile forced."""
+    """Every prefill test runs with the per-shape tile choice, with each tile forced, and
+    with the persistent kernel (one CTA per SM over all tiles)."""
+    if request.param == "persistent":
+        old = tl.set_option(tl.OPT_GEMM_PERSISTENT, 2)
+        yield request.param
+        tl.set_option(tl.OPT_GEMM_PERSISTENT, old)
+        return
     old = tl.set_option(tl.OPT_GEMM_TILE_M, request.param)
     yield request.param
     tl.set_option(tl.OPT_GEMM_TILE_M, old)

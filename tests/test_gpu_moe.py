@@ -53,9 +53,16 @@ def expert_weights(rng, E, K, N, bf16):
     return B, S
 
 
+@pytest.fixture(params=[0, 1], ids=["one_cta_per_tile", "persistent"])
+def persistent(request, tl):
+    old = tl.set_option(tl.OPT_GEMM_PERSISTENT, request.param)
+    yield request.param
+    tl.set_option(tl.OPT_GEMM_PERSISTENT, old)
+
+
 @pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("postop,out_f32", [(0, False), (1, False), (0, True)])
-def test_grouped_gemm(cuda, tl, bf16, postop, out_f32):
+def test_grouped_gemm(cuda, tl, persistent, bf16, postop, out_f32):
     rng = np.random.default_rng(10 + postop)
     T, topk, E, K, N = 400, 4, 12, 512, 272
     ids = routing(rng, T, topk, E, skew=True)
@@ -78,7 +85,7 @@ def test_grouped_gemm(cuda, tl, bf16, postop, out_f32):
 
 
 @pytest.mark.parametrize("bf16", [0, 1])
-def test_layer_vs_token_reference(cuda, tl, bf16):
+def test_layer_vs_token_reference(cuda, tl, persistent, bf16):
     # prefill.cpp's layer: up = gemm(Xs, Bu), H = gemm(Xs, Bg, POSTOP 1, Other = up),
     # Y = gemm(H, Bd, OUT_F32), O = combine(Y)
     import torch

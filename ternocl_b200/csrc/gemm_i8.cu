@@ -8,8 +8,8 @@
 // compute_gold, int2_via_int2_x_int8_dpas/main.cpp:94-121).
 //
 // CTA tile 128 (M) x 128 (N); one stage = one 128-row group (K = 128).  448 threads:
-//   warp 0      producer: Aq [128 x 128] through a 2-D tensor map (8 no-swizzle K-major
-//               boxes of 128 rows x 16 bytes), the group's 8 packed word rows, the SB row
+//   warp 0      producer: Aq [128 x 128] through a 2-D tensor map (one box of 128 rows x
+//               128 bytes in the 128-byte swizzle layout), the group's 8 packed word rows, the SB row
 //               and the tile's SA entries through 1-D bulk copies (3 stages);
 //   warp 1      TMEM (2 x 128 int32 columns) and the MMA issuer: per group four
 //               tcgen05.mma.cta_group::1.kind::i8 (M=128, N=128, K=32, s8 x s8 -> s32)
@@ -38,7 +38,7 @@ constexpr int BM = 128, BN = 128, BK = 128;
 constexpr int kStages = 3, kDecStages = 2;
 constexpr int kDecWarps = 4, kEpiWarps = 8;
 constexpr int kThreads = (2 + kDecWarps + kEpiWarps) * 32;
-constexpr int kALBO = BM * 16, kASBO = 128, kAStageBytes = BM * BK;  // int8 A
+constexpr int kAStageBytes = BM * BK;  // int8 A: one 128-byte-swizzled box of 128 rows x 128 B
 constexpr int kDecLBO = 128, kDecSBO = BK / 16 * 128 + 16;            // 1040
 constexpr int kDecStageBytes = (BN / 8) * kDecSBO;                     // 16640
 constexpr int kPackStageBytes = (BK / 16) * BN * 4;                    // 4096
@@ -52,7 +52,7 @@ struct Smem {
     static constexpr int sb = pack + kStages * kPackStageBytes;
     static constexpr int sa = sb + kStages * kSbBytes;
     static constexpr int bars = sa + kStages * kSaBytes;
-    static constexpr int total = bars + 256;
+    static constexpr int total = bars + 256 + 1024;  // + alignment slack
 };
 
 struct Params {
@@ -109,6 +109,13 @@ __device__ __forceinline__ uint4 s8_row(uint32_t x) {
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// K-major operand in the 128-byte swizzle layout of CU_TENSOR_MAP_SWIZZLE_128B (rows of
+// 128 bytes, 16-byte chunks permuted by row % 8, 8-row groups 1024 B apart; layout type 2)
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+
 // int32 -> fp32 for |d| < 2^22 in two full-rate instructions
 __device__ __forceinline__ float i2f_small(uint32_t d) {
     return __int_as_float((int)(d + 0x4B400000u)) - 12582912.0f;
@@ -116,7 +123,9 @@ __device__ __forceinline__ float i2f_small(uint32_t d) {
 
 template <class DT, int POSTOP, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, const __grid_constant__ CUtensorMap tmA) {
-    extern __shared__ __align__(1024) char smem[];
+    extern __shared__ __align__(1024) char smem_raw[];
+    // 1024-byte aligned base (the 128-byte swizzle pattern is anchored at 1024 B)
+    char *smem = smem_raw + ((1024u - (tc::smem_addr(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int nk = p.K / BK;
@@ -161,8 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
                 if (kb >= kStages && !tc::mbar_wait(&load_empty[s], ((kb / kStages) - 1) & 1)) break;
                 tc::mbar_expect_tx(&full[s], kAStageBytes + pack_bytes + sb_bytes + sa_bytes);
                 char *a = smem + Smem::a + s * kAStageBytes;
-#pragma unroll
-                for (int c = 0; c < BK / 16; ++c) tma_load_2d(a + c * kALBO, &tmA, kb * BK + 16 * c, m0, &full[s]);
+                tma_load_2d(a, &tmA, kb * BK, m0, &full[s]);
                 char *pk = smem + Smem::pack + s * kPackStageBytes;
                 for (int r = 0; r < BK / 16; ++r)
                     tc::bulk_g2s(pk + r * (BN * 4), p.B + (size_t)(kb * (BK / 16) + r) * p.N + n0, ncols * 4, &full[s]);
@@ -186,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
                 const uint32_t bb = tc::smem_addr(smem + Smem::dec + d * kDecStageBytes);
 #pragma unroll
                 for (int kk = 0; kk < BK / 32; ++kk) {
-                    const uint64_t ad = tc::sdesc_kmajor_noswz(a + kk * 2 * kALBO, kALBO, kASBO);
+                    const uint64_t ad = sdesc_kmajor_sw128(a + kk * 32);
                     const uint64_t bd = tc::sdesc_kmajor_noswz(bb + kk * 2 * kDecLBO, kDecLBO, kDecSBO);
                     mma_ss_i8(tmem + b * BN, ad, bd, idesc, kk != 0);
                 }
@@ -305,10 +313,10 @@ cudaError_t int8_gemm_tc_launch(const GemvArgs &a) {
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
     const cuuint64_t strides[1] = {(cuuint64_t)a.K};
-    const cuuint32_t box[2] = {16, BM};
+    const cuuint32_t box[2] = {BK, BM};
     const cuuint32_t estr[2] = {1, 1};
     if (fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(a.Aq), dims, strides, box, estr,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     Params p;

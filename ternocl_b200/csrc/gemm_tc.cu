@@ -669,7 +669,8 @@ static bool use_256_rows(int M, int N) {
     const long long nt = (N + BN - 1) / BN;
     const long long w1 = ((M + BM - 1) / BM * nt + sms - 1) / sms;
     const long long w2 = ((M + 2 * BM - 1) / (2 * BM) * nt + sms - 1) / sms;
-    return w2 * 16 < w1 * 10;
+    // a 256-row tile costs ~1.45x a 128-row one (the B decode is shared by two MMAs)
+    return w2 * 16 < w1 * 11;
 }
 }  // namespace gemm
 

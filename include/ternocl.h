@@ -211,7 +211,9 @@ int ternocl_int2_int8_group_dots(const int8_t *Aq, const uint32_t *B, int32_t *D
  * (bit c of word (kp,n) = weight(32kp+c, n) != 0) | offsets [N] (first sign word of
  * column n) | signs (one bit per non-zero, column-major in k, 1 -> -1) | pad
  * (common/bitcos.hpp:1-8).  SR = slice_ranks [(ls-1), N] for ls K-slices (may be NULL
- * when ls == 1).  Requires N % 16 == 0, K % 128 == 0, K % (64 * ls) == 0. */
+ * when ls == 1).  Requires N % 16 == 0, K % 128 == 0, K % (64 * ls) == 0.  algo: GEMV,
+ * GEMM (the M-tiled tcgen05 kernel; walks all of K per tile, so ls and SR are not read),
+ * or AUTO (GEMM from M >= 64). */
 int ternocl_bitcos_upcvt(const void *A, const uint32_t *B, const void *S, const uint32_t *SR,
                          int ls, void *C, const void *Other, const void *Bias, int M, int N, int K,
                          int dtype, int postop, int out_f32, int algo, void *stream);

@@ -270,6 +270,8 @@ int ternocl_device_error(int reset) {
     v |= t;
     if (read_device_error_allgather(&t, reset) != cudaSuccess) return -1;
     v |= t;
+    if (read_device_error_gemm_bitcos(&t, reset) != cudaSuccess) return -1;
+    v |= t;
     return (int)v;
 }
 
@@ -343,6 +345,11 @@ int ternocl_bitcos_upcvt(const void *A, const uint32_t *B, const void *S, const 
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.SR = SR; a.ls = ls;
     a.stream = (cudaStream_t)stream;
+    // the M-tiled kernel walks all of K per tile: LS and SR do not apply
+    // (bitcos_fp16_upcvt.cl:279-368; the reference selects it with --mt-m, our dispatch at
+    // M >= kGemmMinM)
+    if (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM))
+        return cuda_status(bitcos_gemm_tc_launch(a));
     // no workspace in this signature: split-K stays within one thread-block cluster
     const GemvPlan p = gemv_bitcos_plan(M, N, K, false);
     if (bitcos_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;

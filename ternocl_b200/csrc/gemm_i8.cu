@@ -65,14 +65,6 @@ struct Params {
     int M, N, K, ldsa;
 };
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
-            tc::smem_addr(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(tc::smem_addr(bar))
-        : "memory");
-}
-
 __device__ __forceinline__ void mma_ss_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
     asm volatile(
@@ -107,13 +99,6 @@ __device__ __forceinline__ uint4 s8_row(uint32_t x) {
     }
     transpose4x4(r, o);  // o[q] byte i: row 4q + i
     return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-// K-major operand in the 128-byte swizzle layout of CU_TENSOR_MAP_SWIZZLE_128B (rows of
-// 128 bytes, 16-byte chunks permuted by row % 8, 8-row groups 1024 B apart; layout type 2)
-__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           (1ull << 46) | (2ull << 61);
 }
 
 // int32 -> fp32 for |d| < 2^22 in two full-rate instructions
@@ -170,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
                 if (kb >= kStages && !tc::mbar_wait(&load_empty[s], ((kb / kStages) - 1) & 1)) break;
                 tc::mbar_expect_tx(&full[s], kAStageBytes + pack_bytes + sb_bytes + sa_bytes);
                 char *a = smem + Smem::a + s * kAStageBytes;
-                tma_load_2d(a, &tmA, kb * BK, m0, &full[s]);
+                tc::tma_load_2d(a, &tmA, kb * BK, m0, &full[s]);
                 char *pk = smem + Smem::pack + s * kPackStageBytes;
                 for (int r = 0; r < BK / 16; ++r)
                     tc::bulk_g2s(pk + r * (BN * 4), p.B + (size_t)(kb * (BK / 16) + r) * p.N + n0, ncols * 4, &full[s]);
@@ -194,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
                 const uint32_t bb = tc::smem_addr(smem + Smem::dec + d * kDecStageBytes);
 #pragma unroll
                 for (int kk = 0; kk < BK / 32; ++kk) {
-                    const uint64_t ad = sdesc_kmajor_sw128(a + kk * 32);
+                    const uint64_t ad = tc::sdesc_kmajor_sw128(a + kk * 32);
                     const uint64_t bd = tc::sdesc_kmajor_noswz(bb + kk * 2 * kDecLBO, kDecLBO, kDecSBO);
                     mma_ss_i8(tmem + b * BN, ad, bd, idesc, kk != 0);
                 }
@@ -285,40 +270,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
     }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void *f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)f;
-    }
-    return fn;
-}
-
 }  // namespace gemm8
 
 // Aq [M, K] int8 row-major, SA [K/128, ldsa]
 cudaError_t int8_gemm_tc_launch(const GemvArgs &a) {
     using namespace gemm8;
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return cudaErrorNotSupported;
     CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-    const cuuint64_t strides[1] = {(cuuint64_t)a.K};
-    const cuuint32_t box[2] = {BK, BM};
-    const cuuint32_t estr[2] = {1, 1};
-    if (fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(a.Aq), dims, strides, box, estr,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return cudaErrorInvalidValue;
+    const cudaError_t me = tc::make_map_sw128(&map, a.Aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.M, a.K, BM);
+    if (me != cudaSuccess) return me;
     Params p;
     p.B = a.B;
     p.SB = (const uint16_t *)a.S;

@@ -9,10 +9,10 @@
 //
 // CTA tile 256 (M; 128 for M <= 128 and for MoE row tiles) x 256 (N), K in steps of
 // 64; 320 threads in three roles:
-//   warp 0      TMA producer: A [rows x 64] through a 2-D tensor map (8 boxes of rows x
-//               16 bytes = the no-swizzle K-major core-matrix layout), the packed
-//               weight rows and the scale row through 1-D bulk copies, all completing
-//               on one mbarrier per stage (3-4 load stages);
+//   warp 0      TMA producer: A [rows x 64] through a 2-D tensor map (one box in the
+//               128-byte swizzle layout), the packed weight rows and the scale row
+//               through 1-D bulk copies, all completing on one mbarrier per stage (3-4
+//               load stages);
 //   warp 1      TMEM allocation (256 fp32 columns per 128-row half) and the MMA
 //               issuer: per stage and half four tcgen05.mma.cta_group::1.kind::f16
 //               (M=128, N=256, K=16), A and B from shared-memory descriptors (both
@@ -88,32 +88,6 @@ struct Params {
     const int *meta;
     int E;
 };
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
-            tc::smem_addr(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(tc::smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_ss_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-
-// Shared-memory descriptor of a K-major operand in the 128-byte swizzle layout written by
-// TMA with CU_TENSOR_MAP_SWIZZLE_128B: rows of 64 16-bit elements (128 B), the 16-byte
-// chunks of row r permuted by r % 8, 8-row groups 1024 B apart (SBO), the tile based at a
-// 1024-byte boundary; layout type 2 (SWIZZLE_128B) in bits 61-63, version 1.  A K=16
-// slice of the MMA starts 32 B further into the row.
-__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           (1ull << 46) | (2ull << 61);
-}
 
 template <class DT>
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
@@ -260,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
                 if (kb >= kLoadStages && !tc::mbar_wait(&load_empty[s], ((kb / kLoadStages) - 1) & 1)) break;
                 tc::mbar_expect_tx(&full[s], C::kAStageBytes + pack_bytes + scale_bytes);
                 char *a = smem + C::a + s * C::kAStageBytes;
-                tma_load_2d(a, &tmA, kb * BK, m0, &full[s]);
+                tc::tma_load_2d(a, &tmA, kb * BK, m0, &full[s]);
                 char *pk = smem + C::pack + s * kPackStageBytes;
                 for (int r = 0; r < Policy::kRowsPerStage; ++r)
                     tc::bulk_g2s(pk + r * (BN * 4), Policy::row_ptr(p, kb, r, n0), pack_bytes / Policy::kRowsPerStage,
@@ -290,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
 #pragma unroll
                     for (int h = 0; h < HALVES; ++h) {
                         // rows 128h .. 128h+127 of the A stage: 16 core matrices from h * 2048
-                        const uint64_t ad = sdesc_kmajor_sw128(a + h * BM * 128 + kk * 32);
-                        mma_ss_f16(tmem + h * BN, ad, bd, idesc, (kb | kk) != 0);
+                        const uint64_t ad = tc::sdesc_kmajor_sw128(a + h * BM * 128 + kk * 32);
+                        tc::mma_ss_f16(tmem + h * BN, ad, bd, idesc, (kb | kk) != 0);
                     }
                 }
                 tc::mma_commit(&load_empty[s]);
@@ -453,7 +427,7 @@ __global__ void __launch_bounds__(kPThreads, 1) gemm_persistent_kernel(const Par
                     }
                     tc::mbar_expect_tx(&full[s], C::kAStageBytes + pack_bytes + scale_bytes);
                     char *a = smem + C::a + s * C::kAStageBytes;
-                    tma_load_2d(a, &tmA, kb * BK, ti.m0, &full[s]);
+                    tc::tma_load_2d(a, &tmA, kb * BK, ti.m0, &full[s]);
                     char *pk = smem + C::pack + s * kPackStageBytes;
                     for (int r = 0; r < Policy::kRowsPerStage; ++r)
                         tc::bulk_g2s(pk + r * (BN * 4), Policy::row_ptr(q, kb, r, ti.n0),
@@ -487,8 +461,8 @@ __global__ void __launch_bounds__(kPThreads, 1) gemm_persistent_kernel(const Par
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t bd = tc::sdesc_kmajor_noswz(bb + kk * 2 * kDecLBO, kDecLBO, kDecSBO);
-                        const uint64_t ad = sdesc_kmajor_sw128(a + kk * 32);
-                        mma_ss_f16(tmem + b * BN, ad, bd, idesc, (kb | kk) != 0);
+                        const uint64_t ad = tc::sdesc_kmajor_sw128(a + kk * 32);
+                        tc::mma_ss_f16(tmem + b * BN, ad, bd, idesc, (kb | kk) != 0);
                     }
                     tc::mma_commit(&load_empty[s]);
                     tc::mma_commit(&dec_empty[d]);
@@ -560,39 +534,11 @@ __global__ void __launch_bounds__(kPThreads, 1) gemm_persistent_kernel(const Par
     }
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void *f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)f;
-    }
-    return fn;
-}
-
 // A [M, K] DT row-major; boxes of box_rows rows x 64 elements in the 128-byte swizzle
 // layout, rows past M read as zero
 static cudaError_t make_map_a(CUtensorMap *map, const void *A, int M, int K, bool bf16, int box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return cudaErrorNotSupported;
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                          const_cast<void *>(A), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+    return tc::make_map_sw128(map, A, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                              M, K, box_rows);
 }
 
 template <class Policy>
@@ -661,7 +607,7 @@ namespace gemm {
 // 128- or 256-row tiles: one CTA per SM, so a grid runs in ceil(tiles / SMs) waves; a
 // 256-row tile does twice the work of a 128-row one in ~1.6x the time (measured on
 // B200), so pick the shape with fewer wave-weighted units.  MoE tiles are 128 rows.
-static bool use_256_rows(int M, int N) {
+bool use_256_rows(int M, int N) {
     if (options().gemm_tile_m) return options().gemm_tile_m == 256;
     if (M <= BM) return false;
     int dev = 0, sms = 148;
@@ -673,6 +619,8 @@ static bool use_256_rows(int M, int N) {
     return w2 * 16 < w1 * 11;
 }
 }  // namespace gemm
+
+bool gemm_use_256_rows(int M, int N) { return gemm::use_256_rows(M, N); }
 
 cudaError_t int2_gemm_tc_launch(const GemvArgs &a) {
     if (options().gemm_persistent == 2) return gemm::launch_persistent<gemm::Int2Gemm>(a);

@@ -138,6 +138,11 @@ cudaError_t read_device_error_gemv_tc(unsigned *out, int reset);
 cudaError_t int2_gemm_tc_launch(const GemvArgs &a);
 cudaError_t int1_gemm_tc_launch(const GemvArgs &a);
 cudaError_t read_device_error_gemm_tc(unsigned *out, int reset);
+// 256-row (two 128-row MMAs sharing the decoded B) rather than 128-row GEMM tiles
+bool gemm_use_256_rows(int M, int N);
+// BITCOS prefill GEMM (gemm_bitcos.cu): a.B = the whole BITCOS buffer, no K split
+cudaError_t bitcos_gemm_tc_launch(const GemvArgs &a);
+cudaError_t read_device_error_gemm_bitcos(unsigned *out, int reset);
 // s8 x s2 prefill GEMM (gemm_i8.cu): a.Aq int8 [M, K], a.SA [K/128, ldsa], a.S = SB
 cudaError_t int8_gemm_tc_launch(const GemvArgs &a);
 cudaError_t read_device_error_gemm_i8(unsigned *out, int reset);

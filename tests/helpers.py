@@ -10,14 +10,19 @@ from ternocl_b200 import synth
 # is bounded by the fp32 accumulation error of the much larger partial sums).
 REL_TOL = {0: 2e-3, 1: 1e-2}
 # fp32 outputs differ from the gold only by the fp32 reduction order; the reference's
-# own rule for them is rel <= 2e-4 (compare_f32, common/epilogue.hpp:69-77)
+# own rule for them is, per element, rel <= 2e-4 or |d| <= 0.05 (compare_f32,
+# common/epilogue.hpp:69-84).  Its absolute 0.05 is ~5e-5 of the outputs' scale under
+# the reference drivers' input distributions; the fp32 rule here keeps that ratio with a
+# floor of 0.25 rms(gold) (2e-4 x 0.25 rms = 5e-5 rms), far above the fp32 summation
+# noise (~sqrt(K) 2^-24 rms) and far below what a wrong term would give.
 F32_REL_TOL = 2e-4
+F32_FLOOR = 0.25
 
 
-def rel_err(out, gold):
+def rel_err(out, gold, floor_frac=1e-2):
     out = np.asarray(out, np.float64)
     gold = np.asarray(gold, np.float64)
-    floor = 1e-2 * max(np.sqrt(np.mean(gold ** 2)), 1e-30)
+    floor = floor_frac * max(np.sqrt(np.mean(gold ** 2)), 1e-30)
     return np.max(np.abs(out - gold) / np.maximum(np.abs(gold), floor)) if gold.size else 0.0
 
 
@@ -30,7 +35,7 @@ def ulp_diff(a, b):
 def check_output(out, gold, bf16, out_f32, what=""):
     """out/gold: raw DT bits (uint16) or fp32. Asserts the tolerance and returns stats."""
     if out_f32:
-        e = rel_err(out, gold)
+        e = rel_err(out, gold, F32_FLOOR)
         assert e <= F32_REL_TOL, "%s fp32 rel err %.3g > %.3g" % (what, e, F32_REL_TOL)
         return e
     o = synth.from_dt(out, bf16)

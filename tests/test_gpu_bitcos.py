@@ -1,4 +1,4 @@
-"""BITCOS GEMV on the GPU vs the oracle (the reference's host gold,
+"""BITCOS GEMV and M-tiled GEMM on the GPU vs the oracle (the reference's host gold,
 bitcos_fp16_upcvt/main.cpp:64-86 with bitcos_decode_col, common/bitcos.hpp:97-106,
 + the epilogue), through the C ABI.  Buffers come from the library's host packer,
 which reproduces bitcos_random (common/bitcos.hpp:31-78) bit for bit."""
@@ -34,7 +34,7 @@ def gold_out(c, M, K, N, bf16, postop, out_f32):
     return orc.epilogue(postop, out_f32, acc, c["other"], c["bias"], M, N, bf16)
 
 
-def run(tl, c, K, N, bf16, ls, postop=0, out_f32=False):
+def run(tl, c, K, N, bf16, ls, postop=0, out_f32=False, algo=0):
     import torch
     A, B, S = dev_dt(c["A"], bf16), dev_words(c["buf"]), dev_dt(c["S"], bf16)
     SR = dev_words(tl.bitcos_slice_ranks(c["buf"], K, N, ls)) if ls > 1 else None
@@ -42,7 +42,7 @@ def run(tl, c, K, N, bf16, ls, postop=0, out_f32=False):
     bias = None
     if c["bias"] is not None:
         bias = torch.from_numpy(c["bias"]).cuda() if out_f32 else dev_dt(c["bias"], bf16)
-    out = tl.bitcos_upcvt(A, B, S, SR=SR, ls=ls, postop=postop, out_f32=out_f32, other=other, bias=bias)
+    out = tl.bitcos_upcvt(A, B, S, SR=SR, ls=ls, postop=postop, out_f32=out_f32, other=other, bias=bias, algo=algo)
     return host_dt(out)
 
 
@@ -119,3 +119,79 @@ def test_shape_errors(cuda, tl):
     assert L.ternocl_bitcos_upcvt(p(A), p(B), p(S), p(B), 3, p(C), None, None, 1, 48, 256, 0, 0, 0, 0, None) == 1
     # ls > 1 needs slice ranks
     assert L.ternocl_bitcos_upcvt(p(A), p(B), p(S), None, 2, p(C), None, None, 1, 48, 256, 0, 0, 0, 0, None) == 2
+
+
+# ---- M-tiled tcgen05 GEMM (bitcos_fp16_upcvt_gemm_mt, bitcos_fp16_upcvt.cl:279-368) ----
+GEMM = 2
+
+
+@pytest.fixture(params=[128, 256], ids=["tile128", "tile256"])
+def tile_m(request, tl):
+    old = tl.set_option(tl.OPT_GEMM_TILE_M, request.param)
+    yield request.param
+    tl.set_option(tl.OPT_GEMM_TILE_M, old)
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("z", [0.2, 0.5])
+@pytest.mark.parametrize("M,K,N", [(512, 5376, 512), (64, 1024, 256), (200, 2048, 272), (1, 256, 48),
+                                   (300, 5376, 784), (129, 128, 16)])
+def test_gemm_parity(cuda, tl, tile_m, M, K, N, z, bf16):
+    c = case(tl, 900 + M + K + N + int(100 * z), M, K, N, z, bf16)
+    gold = gold_out(c, M, K, N, bf16, 0, False)
+    check_output(run(tl, c, K, N, bf16, 1, algo=GEMM), gold, bf16, False,
+                 "bitcos gemm M=%d K=%d N=%d z=%.2f bf16=%d" % (M, K, N, z, bf16))
+
+
+@pytest.mark.parametrize("z", [0.0, 0.95, 1.0])
+def test_gemm_density_extremes(cuda, tl, z):
+    M, K, N = 96, 2048, 384
+    c = case(tl, 43, M, K, N, z, 0)
+    gold = gold_out(c, M, K, N, 0, 0, False)
+    check_output(run(tl, c, K, N, 0, 1, algo=GEMM), gold, 0, False, "gemm z=%.2f" % z)
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("postop", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("out_f32", [False, True])
+def test_gemm_epilogues(cuda, tl, bf16, postop, out_f32):
+    M, K, N = 160, 1024, 528
+    c = case(tl, 80 + postop, M, K, N, 0.35, bf16, postop, out_f32)
+    gold = gold_out(c, M, K, N, bf16, postop, out_f32)
+    check_output(run(tl, c, K, N, bf16, 1, postop, out_f32, algo=GEMM), gold, bf16, out_f32,
+                 "gemm postop=%d out_f32=%d" % (postop, out_f32))
+
+
+def test_gemm_decode_bit_exact(cuda, tl, tile_m):
+    # A = identity (M = K = 512, so AUTO picks the GEMM): C = the decoded weights
+    K, N = 512, 96
+    buf = tl.bitcos_random(K, N, 0.35, 5)
+    S = synth.to_dt(np.ones((K // 128, N)), 0)
+    eye = synth.to_dt(np.eye(K), 0)
+    c = dict(A=eye, buf=buf, S=S, other=None, bias=None)
+    out = synth.from_dt(run(tl, c, K, N, 0, 1), 0)
+    assert np.array_equal(out, orc.bitcos_decode(buf, K, N).T.astype(np.float32))
+    assert tl.device_error() == 0
+
+
+def test_gemm_golden(cuda, tl):
+    d = np.load(GOLDEN)
+    for zk in ("z35", "z05", "z95"):
+        buf = d["bitcos_%s_buf" % zk]
+        for dt, bf16 in (("fp16", 0), ("bf16", 1)):
+            A, S = d["bitcos_%s_%s_A" % (zk, dt)], d["bitcos_%s_%s_S" % (zk, dt)]
+            M, K = A.shape
+            N = S.shape[1]
+            gold = orc.epilogue(0, False, d["bitcos_%s_%s_acc" % (zk, dt)], None, None, M, N, bf16)
+            c = dict(A=A, buf=buf, S=S, other=None, bias=None)
+            check_output(run(tl, c, K, N, bf16, 1, algo=GEMM), gold, bf16, False, "gemm %s %s" % (zk, dt))
+
+
+def test_gemm_matches_gemv(cuda, tl):
+    # same inputs through both kernels: identical up to fp32 summation order
+    M, K, N = 8, 5376, 1024
+    c = case(tl, 77, M, K, N, 0.35, 1)
+    a = synth.from_dt(run(tl, c, K, N, 1, 1, algo=GEMM), 1)
+    b = synth.from_dt(run(tl, c, K, N, 1, 4, algo=1), 1)
+    gold = synth.from_dt(gold_out(c, M, K, N, 1, 0, False), 1)
+    assert np.max(np.abs(a - b)) <= np.max(np.abs(gold)) * 2e-2

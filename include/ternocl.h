@@ -91,13 +91,17 @@ int ternocl_device_error(int reset);
  *    SM over all tiles, epilogue overlapped with the next tile) for 0 = no GEMM,
  *    1 = the MoE grouped GEMMs, 2 = every prefill GEMM (measured slower than one CTA
  *    per tile on B200 for the shapes benchmarked here).
+ *  TERNOCL_OPT_GEMV_IMPL (default 0 = chosen per M): the int2 decode GEMV used by
+ *    ternocl_int2_upcvt at small M: 1 = fp16/bf16 MMA on decoded weights, 2 = integer
+ *    MMA on int8 weights and exact 24-bit fixed-point activations (M <= 4).
  * Returns the previous value, or -1 for an unknown option or value. */
 typedef enum {
     TERNOCL_OPT_PDL = 1,
     TERNOCL_OPT_GEMM_TILE_M = 2,
     TERNOCL_OPT_GEMV_SPLIT = 3,
     TERNOCL_OPT_GEMV_WARPS = 4,
-    TERNOCL_OPT_GEMM_PERSISTENT = 5
+    TERNOCL_OPT_GEMM_PERSISTENT = 5,
+    TERNOCL_OPT_GEMV_IMPL = 6
 } ternocl_option;
 int ternocl_set_option(int option, int value);
 

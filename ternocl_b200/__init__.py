@@ -17,6 +17,7 @@ OPT_GEMM_TILE_M = 2
 OPT_GEMV_SPLIT = 3
 OPT_GEMV_WARPS = 4
 OPT_GEMM_PERSISTENT = 5
+OPT_GEMV_IMPL = 6
 
 
 def _torch():

@@ -176,9 +176,12 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
     a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.stream = (cudaStream_t)stream;
+    const int impl = options().gemv_impl;
+    const bool digit = M <= kGemvDigitMaxM && (impl == 2 || impl == 0);
     GemvPlan p = gemv_plan(M, N, K, ws != nullptr);
     if (p.total() > ws_bytes) p = gemv_plan(M, N, K, false);
-    if (int2_gemv_smem(M, K, p.SK, p.warps) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    const size_t smem = digit ? int2_gemv_d_smem(M, K, p.SK, p.warps) : int2_gemv_smem(M, K, p.SK, p.warps);
+    if (smem > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
     a.SK = p.SK;
     a.warps = p.warps;
     a.cluster = p.cluster ? 1 : 0;
@@ -187,7 +190,7 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
         a.ws_cnt = (unsigned *)ws;
         a.ws_part = (float *)((char *)ws + p.cnt_bytes);
     }
-    return cuda_status(int2_gemv_launch(a));
+    return cuda_status(digit ? int2_gemv_d_launch(a) : int2_gemv_launch(a));
 }
 int report_cuda(cudaError_t e) { return cuda_status(e); }
 
@@ -237,6 +240,12 @@ int ternocl_set_option(int option, int value) {
         if (value < 0 || value > 64) return -1;
         const int old = options().gemv_split;
         options().gemv_split = value;
+        return old;
+    }
+    if (option == TERNOCL_OPT_GEMV_IMPL) {
+        if (value < 0 || value > 2) return -1;
+        const int old = options().gemv_impl;
+        options().gemv_impl = value;
         return old;
     }
     if (option == TERNOCL_OPT_GEMM_TILE_M) {

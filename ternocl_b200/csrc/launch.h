@@ -20,6 +20,7 @@ struct Options {
     int gemv_split = 0;   // decode GEMV K split: 0 = planned per shape
     int gemv_warps = 0;   // decode GEMV warps per CTA: 0 = planned per shape
     int gemm_persistent = 0;  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every prefill GEMM
+    int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA (M <= 4)
 };
 Options &options();
 
@@ -129,6 +130,10 @@ size_t int1_gemv_smem(int M, int K, int SK);
 size_t int8_gemv_smem(int M, int K, int SK);
 cudaError_t int2_gemv_launch(const GemvArgs &a);
 size_t int2_gemv_smem(int M, int K, int SK, int warps = 4);
+// int2 GEMV on integer MMAs (gemv_i2d.cu): 32 columns x <= 4 rows per CTA
+constexpr int kGemvDigitMaxM = 4;
+cudaError_t int2_gemv_d_launch(const GemvArgs &a);
+size_t int2_gemv_d_smem(int M, int K, int SK, int warps);
 // tcgen05 / TMEM decode GEMV (gemv_tc.cu): 128 columns and tc_gemv_rows(M) rows per CTA
 int tc_gemv_rows(int M);
 size_t int2_gemv_tc_smem(int M, int K, int SK);

@@ -93,7 +93,9 @@ int ternocl_device_error(int reset);
  *    per tile on B200 for the shapes benchmarked here).
  *  TERNOCL_OPT_GEMV_IMPL (default 0 = chosen per M): the int2 decode GEMV used by
  *    ternocl_int2_upcvt at small M: 1 = fp16/bf16 MMA on decoded weights, 2 = integer
- *    MMA on int8 weights and exact 24-bit fixed-point activations (M <= 4).
+ *    MMA on int8 weights and exact fixed-point activations (M <= 4, the default there),
+ *    3 = the same arithmetic in a persistent kernel fed by TMA with a stream-K split
+ *    (M = 1; measured slower than 2 on B200, so opt-in).
  * Returns the previous value, or -1 for an unknown option or value. */
 typedef enum {
     TERNOCL_OPT_PDL = 1,

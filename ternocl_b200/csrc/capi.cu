@@ -177,7 +177,18 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.stream = (cudaStream_t)stream;
     const int impl = options().gemv_impl;
-    const bool digit = M <= kGemvDigitMaxM && (impl == 2 || impl == 0);
+    if (M == 1 && !peer && impl == 3) {
+        // persistent TMA-streamed GEMV; its stream-K split needs the workspace
+        const size_t need = int2_gemv_p_workspace(N);
+        if (ws && ws_bytes >= need) {
+            if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
+            const int tiles = (N + 127) / 128;
+            a.ws_cnt = (unsigned *)ws;
+            a.ws_part = (float *)((char *)ws + round_up((size_t)tiles * 4, 256));
+        }
+        return cuda_status(int2_gemv_p_launch(a));
+    }
+    const bool digit = M <= kGemvDigitMaxM && impl != 1;
     GemvPlan p = gemv_plan(M, N, K, ws != nullptr);
     if (p.total() > ws_bytes) p = gemv_plan(M, N, K, false);
     const size_t smem = digit ? int2_gemv_d_smem(M, K, p.SK, p.warps) : int2_gemv_smem(M, K, p.SK, p.warps);
@@ -243,7 +254,7 @@ int ternocl_set_option(int option, int value) {
         return old;
     }
     if (option == TERNOCL_OPT_GEMV_IMPL) {
-        if (value < 0 || value > 2) return -1;
+        if (value < 0 || value > 3) return -1;
         const int old = options().gemv_impl;
         options().gemv_impl = value;
         return old;
@@ -264,6 +275,7 @@ size_t ternocl_gemv_workspace_size(int M, int N, int K) {
     const size_t b = gemv_tc_plan(M, N, K, true).total(), c = gemv_i1_plan(M, N, K, true).total();
     if (b > need) need = b;
     if (c > need) need = c;
+    if (M == 1 && int2_gemv_p_workspace(N) > need) need = int2_gemv_p_workspace(N);
     return need;
 }
 
@@ -280,6 +292,8 @@ int ternocl_device_error(int reset) {
     if (read_device_error_allgather(&t, reset) != cudaSuccess) return -1;
     v |= t;
     if (read_device_error_gemm_bitcos(&t, reset) != cudaSuccess) return -1;
+    v |= t;
+    if (read_device_error_gemv_p(&t, reset) != cudaSuccess) return -1;
     v |= t;
     return (int)v;
 }

@@ -20,7 +20,7 @@ struct Options {
     int gemv_split = 0;   // decode GEMV K split: 0 = planned per shape
     int gemv_warps = 0;   // decode GEMV warps per CTA: 0 = planned per shape
     int gemm_persistent = 0;  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every prefill GEMM
-    int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA (M <= 4)
+    int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA (M <= 4), 3 persistent (M = 1)
 };
 Options &options();
 
@@ -134,6 +134,11 @@ size_t int2_gemv_smem(int M, int K, int SK, int warps = 4);
 constexpr int kGemvDigitMaxM = 4;
 cudaError_t int2_gemv_d_launch(const GemvArgs &a);
 size_t int2_gemv_d_smem(int M, int K, int SK, int warps);
+// persistent TMA-streamed int2 GEMV for M = 1 (gemv_i2p.cu); a.ws_part / a.ws_cnt (or null)
+// hold its stream-K partials and tile counters
+cudaError_t int2_gemv_p_launch(const GemvArgs &a);
+size_t int2_gemv_p_workspace(int N);
+cudaError_t read_device_error_gemv_p(unsigned *out, int reset);
 // tcgen05 / TMEM decode GEMV (gemv_tc.cu): 128 columns and tc_gemv_rows(M) rows per CTA
 int tc_gemv_rows(int M);
 size_t int2_gemv_tc_smem(int M, int K, int SK);

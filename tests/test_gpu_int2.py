@@ -10,7 +10,8 @@ pytestmark = pytest.mark.gpu
 # shapes from the reference validation matrix (int2_fp16_upcvt/validate.sh:8-10) and
 # the Llama-3-8B decode sweep, at sizes the oracle finishes in seconds
 GEMV_SHAPES = [(1, 4096, 4096), (1, 4096, 6144), (4, 6144, 5120), (3, 256, 48), (8, 1024, 512),
-               (1, 128, 16), (2, 512, 272), (5, 2048, 1024), (13, 512, 256), (1, 14336, 512)]
+               (1, 128, 16), (2, 512, 272), (5, 2048, 1024), (13, 512, 256), (1, 14336, 512),
+               (1, 384, 272), (1, 5376, 2576)]
 
 
 def run(tl, c, M, K, N, bf16, postop, out_f32, algo, ws=None):
@@ -26,15 +27,16 @@ def run(tl, c, M, K, N, bf16, postop, out_f32, algo, ws=None):
 
 
 # GEMV implementations: fp16/bf16 mma.sync on decoded weights, integer mma.sync on int8
-# weights and fixed-point activation digits (M <= 4), tcgen05/TMEM
-ALGOS = ["f16", "digit", "tmem"]
+# weights and fixed-point activation digits (M <= 4), the persistent TMA-fed variant of
+# the latter (M = 1; larger M fall back), tcgen05/TMEM
+ALGOS = ["f16", "digit", "persist", "tmem"]
 
 
 @pytest.fixture
 def gemv_algo(request, tl):
     """Maps an ALGOS name to (algo argument, implementation option) for the test body."""
     def select(name):
-        impl = {"f16": 1, "digit": 2, "tmem": 0}[name]
+        impl = {"f16": 1, "digit": 2, "persist": 3, "tmem": 0}[name]
         old = tl.set_option(tl.OPT_GEMV_IMPL, impl)
         request.addfinalizer(lambda: tl.set_option(tl.OPT_GEMV_IMPL, old))
         return tl.ALGO_GEMV_TMEM if name == "tmem" else tl.ALGO_GEMV

@@ -605,14 +605,35 @@ def main():
     achieved = set_bytes * args.steps / (kern_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
 
-    # end to end through the C ABI with host buffers (pinned), rank-local
+    # end to end through the C ABI with host buffers (pinned), rank-local: per step one
+    # copy of the four activation vectors in (one pinned buffer), the four GEMVs, one copy
+    # of the four outputs out, and a synchronisation (the decode loop reads its result)
     hA = [torch.randn(M, ly["K"]).half().pin_memory() for ly in layers]
     hC = [torch.empty(M, ly["nl"], dtype=torch.float16).pin_memory() for ly in layers]
     h2d = sum(x.numel() * 2 for x in hA)
     d2h = sum(x.numel() * 2 for x in hC)
+    packed = fused is None and world == 1
+    if packed:
+        ka = [ly["K"] * M for ly in layers]
+        kc = [ly["nl"] * M for ly in layers]
+        hAall = torch.cat([x.reshape(-1) for x in hA]).pin_memory()
+        hCall = torch.empty(sum(kc), dtype=torch.float16).pin_memory()
+        dAall = torch.empty(sum(ka), dtype=torch.float16, device=dev)
+        dCall = torch.empty(sum(kc), dtype=torch.float16, device=dev)
+        oa = np.cumsum([0] + ka)
+        oc = np.cumsum([0] + kc)
+        e2e_layers = [dict(ly, A=dAall[oa[j]:oa[j + 1]].view(M, ly["K"]), C=dCall[oc[j]:oc[j + 1]].view(M, ly["nl"]))
+                      for j, ly in enumerate(layers)]
 
     def e2e_step(i):
         s = i % nsets
+        if packed:
+            dAall.copy_(hAall, non_blocking=True)
+            for ly in e2e_layers:
+                gemv(ly, s)
+            hCall.copy_(dCall, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            return
         for j, ly in enumerate(layers):
             ly["A"].copy_(hA[j], non_blocking=True)
             if fused is not None:
@@ -676,7 +697,7 @@ def main():
                        "launch": "one CUDA graph of the K timed steps" if (args.graph and world == 1) else "host calls, PDL"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "kernel": "int2_gemv_kernel", "launches": launches,
+                         "kernel": "gemv_i2d_kernel (integer-MMA int2 GEMV)", "launches": launches,
                          "bytes_per_step": set_bytes,
                          "traffic": tr.get("bytes_per_step") if tr else None},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,

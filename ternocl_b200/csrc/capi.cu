@@ -205,6 +205,38 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
 }
 int report_cuda(cudaError_t e) { return cuda_status(e); }
 
+// (kernel, device) -> dynamic shared memory attribute already set
+namespace {
+struct SmemAttrEntry {
+    const void *fn;
+    int dev, bytes;
+};
+std::mutex g_smem_mu;
+SmemAttrEntry g_smem_attr[1024];
+int g_smem_n = 0;
+}  // namespace
+
+bool smem_attr_known(const void *fn, int bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lock(g_smem_mu);
+    for (int i = 0; i < g_smem_n; ++i)
+        if (g_smem_attr[i].fn == fn && g_smem_attr[i].dev == dev) return g_smem_attr[i].bytes >= bytes;
+    return false;
+}
+
+void smem_attr_record(const void *fn, int bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    std::lock_guard<std::mutex> lock(g_smem_mu);
+    for (int i = 0; i < g_smem_n; ++i)
+        if (g_smem_attr[i].fn == fn && g_smem_attr[i].dev == dev) {
+            if (bytes > g_smem_attr[i].bytes) g_smem_attr[i].bytes = bytes;
+            return;
+        }
+    if (g_smem_n < 1024) g_smem_attr[g_smem_n++] = {fn, dev, bytes};
+}
+
 }  // namespace ternocl
 
 using namespace ternocl;

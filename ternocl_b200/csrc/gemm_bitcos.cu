@@ -316,7 +316,7 @@ cudaError_t launch_h(const GemvArgs &a) {
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
         auto kern = bitcos_gemm_kernel<HALVES, DT, decltype(po)::value, decltype(of)::value>;
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<HALVES>::total);
+        cudaError_t err = ensure_smem(kern, Cfg<HALVES>::total);
         if (err != cudaSuccess) return err;
         const int rows = Cfg<HALVES>::kRows;
         const dim3 grid((a.N + BN - 1) / BN, (a.M + rows - 1) / rows);

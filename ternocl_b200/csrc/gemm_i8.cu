@@ -292,7 +292,7 @@ cudaError_t int8_gemm_tc_launch(const GemvArgs &a) {
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
         auto kern = gemm_i8_kernel<DT, decltype(po)::value, decltype(of)::value>;
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total);
+        cudaError_t err = ensure_smem(kern, Smem::total);
         if (err != cudaSuccess) return err;
         const dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
         return launch_kernel(kern, grid, dim3(kThreads), (size_t)Smem::total, a.stream, p, map);

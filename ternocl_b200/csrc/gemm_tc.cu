@@ -566,7 +566,7 @@ cudaError_t launch_persistent(const GemvArgs &a, const int *meta = nullptr, int 
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
         auto kern = gemm_persistent_kernel<Policy, DT, decltype(po)::value, decltype(of)::value>;
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<1>::total);
+        cudaError_t err = ensure_smem(kern, Cfg<1>::total);
         if (err != cudaSuccess) return err;
         return launch_kernel(kern, dim3(grid), dim3(kPThreads), (size_t)Cfg<1>::total, a.stream, p, map);
     });
@@ -591,7 +591,7 @@ cudaError_t launch_policy(const GemvArgs &a, const int *meta = nullptr, int E = 
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
         auto kern = gemm_kernel<Policy, HALVES, DT, decltype(po)::value, decltype(of)::value>;
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<HALVES>::total);
+        cudaError_t err = ensure_smem(kern, Cfg<HALVES>::total);
         if (err != cudaSuccess) return err;
         // grouped: every expert adds at most one partial row tile
         const int rows = Cfg<HALVES>::kRows;

@@ -319,7 +319,7 @@ cudaError_t launch_w(const GemvArgs &a) {
     const size_t smem = i2d_smem(W, rows, ngw);
     auto kern = gemv_i2d_kernel<W, NMMA, DT, POSTOP, OUT_F32>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess) return e;
     }
     dim3 grid((a.N + kCols - 1) / kCols, a.SK, (a.M + kMaxRows - 1) / kMaxRows);

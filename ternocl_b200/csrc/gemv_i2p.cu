@@ -414,7 +414,7 @@ cudaError_t int2_gemv_p_launch(const GemvArgs &a) {
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
         auto kern = gemv_i2p_kernel<DT, decltype(po)::value, decltype(of)::value>;
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+        cudaError_t err = ensure_smem(kern, kSmemTotal);
         if (err != cudaSuccess) return err;
         return launch_kernel(kern, dim3(p.P), dim3(kThreads), (size_t)kSmemTotal, a.stream, p, mB, mS);
     });

@@ -167,7 +167,7 @@ cudaError_t launch_w(const GemvArgs &a) {
     const size_t smem = gemv::smem_bytes<Int2Policy, W>(rows, max_ng * kGS);
     auto kern = gemv::gemv_kernel<Int2Policy, W, DT, POSTOP, OUT_F32>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess) return e;
     }
     dim3 grid((a.N + 31) / 32, a.SK, (a.M + 7) / 8);

@@ -179,7 +179,7 @@ cudaError_t launch_t(const GemvArgs &a) {
     const size_t smem = gemv::smem_bytes<Int8Policy, gemv::kWarps>(rows, max_ng * kGS);
     auto kern = gemv::gemv_kernel<Int8Policy, gemv::kWarps, DT, POSTOP, OUT_F32>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess) return e;
     }
     dim3 grid((a.N + 31) / 32, a.SK, (a.M + 7) / 8);

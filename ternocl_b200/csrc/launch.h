@@ -82,6 +82,19 @@ cudaError_t dispatch_epilogue(const Args &a, F &&f) {
     return with_dt(type_tag<F16>{});
 }
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per kernel, device and size: the
+// attribute outlives the call, and setting it on every launch costs host time in the
+// decode loop (capi.cu keeps the record).
+bool smem_attr_known(const void *fn, int bytes);
+void smem_attr_record(const void *fn, int bytes);
+template <class F>
+cudaError_t ensure_smem(F *kern, size_t bytes) {
+    if (bytes <= 48 * 1024 || smem_attr_known((const void *)kern, (int)bytes)) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) smem_attr_record((const void *)kern, (int)bytes);
+    return e;
+}
+
 template <class... KArgs, class... Args>
 cudaError_t launch_kernel_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                                   cudaStream_t stream, dim3 cluster, Args &&...args) {

@@ -214,7 +214,7 @@ cudaError_t moe_route_launch(const int *ids, int *meta, int *perm, int *inv, int
     const size_t smem = moe_route_smem(E);
     auto kern = G > kRouteThreads ? moe_route_mc_kernel : moe_route_kernel;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem(kern, smem);
         if (e != cudaSuccess) return e;
     }
     const int ctas = G > kRouteThreads ? (G + kRouteThreads - 1) / kRouteThreads : 1;

@@ -257,6 +257,28 @@ int ternocl_moe_combine(const float *Y, const int32_t *inv, const void *RW, void
                         int topk, int dtype, void *stream);
 
 /* ---------------------------------------------------------------------------------
+ * int2 MoE decode (int2_moe/int2_moe.cl:63-174), every routed (token, expert) pair in one
+ * launch.  ids[G] = expert of row g = t*topk + j; B* [E, K/16, N], S* [E, K/128, N] per
+ * projection (E = num_experts); fp32 accumulation per 128-row group as the int2 GEMV.
+ * An expert id outside [0, E) contributes zero and sets bit 1 of ternocl_device_error.
+ *
+ * gate_up, replaces int2_moe_gate_up (:65-67), X [T, K] with T = G / topk:
+ *   H[g, n] = DT(silu(X[g/topk] . gate_e[:, n]) * (X[g/topk] . up_e[:, n]))   H [G, N] */
+int ternocl_moe_decode_gate_up(const int32_t *ids, const void *X, const uint32_t *Bg, const void *Sg,
+                               const uint32_t *Bu, const void *Su, void *H, int G, int N, int K, int topk,
+                               int num_experts, int dtype, void *stream);
+/* down, replaces int2_moe_down (:103-104): Y[g, n] = RW[g] * (H[g] . down_e[:, n]), Y fp32 [G, N] */
+int ternocl_moe_decode_down(const int32_t *ids, const void *H, const void *RW, const uint32_t *B, const void *S,
+                            float *Y, int G, int N, int K, int num_experts, int dtype, void *stream);
+/* reduce, replaces int2_moe_reduce (:131): O[t, n] = DT(sum_j Y[t*topk + j, n]), j ascending */
+int ternocl_moe_decode_reduce(const float *Y, void *O, int T, int N, int topk, int dtype, void *stream);
+/* down_sum, replaces int2_moe_down_sum (:148-149), down + reduce in one launch:
+ *   O[t, n] = DT(sum_j RW[g] * (H[g] . down_e[:, n])),  g = t*topk + j */
+int ternocl_moe_decode_down_sum(const int32_t *ids, const void *H, const void *RW, const uint32_t *B,
+                                const void *S, void *O, int T, int N, int K, int topk, int num_experts, int dtype,
+                                void *stream);
+
+/* ---------------------------------------------------------------------------------
  * Host-side weight packers (no device work).  Same layouts as the reference's
  * common/bitcos.hpp and int1 driver.
  *

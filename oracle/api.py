@@ -62,6 +62,7 @@ def orc():
             "orc_hadamard": (i, [vp, vp, vp, i, i, i, i, i]),
             "orc_moe_route": (None, [vp, i, i, i, vp, vp, vp]),
             "orc_moe_token_ref": (None, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp, i]),
+            "orc_moe_decode_token_ref": (None, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp, i]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
@@ -243,6 +244,16 @@ def moe_token_ref(X, ids, RW, Bg, Sg, Bu, Su, Bd, Sd, t, topk, H, I, bf16):
             _c(Sd, np.uint16)]
     o = np.zeros(H, np.float64)
     orc().orc_moe_token_ref(*[_p(a) for a in args], t, topk, H, I, _p(o), int(bf16))
+    return o
+
+
+def moe_decode_token_ref(X, ids, RW, Bg, Sg, Bu, Su, Bd, Sd, t, topk, H, I, bf16):
+    """int2_moe/main.cpp:267-291: the decode layer's output for token t (double precision)."""
+    args = [_c(X, np.uint16), _c(ids, np.int32), _c(RW, np.uint16), _c(Bg, np.uint32),
+            _c(Sg, np.uint16), _c(Bu, np.uint32), _c(Su, np.uint16), _c(Bd, np.uint32),
+            _c(Sd, np.uint16)]
+    o = np.zeros(H, np.float64)
+    orc().orc_moe_decode_token_ref(*[_p(a) for a in args], t, topk, H, I, _p(o), int(bf16))
     return o
 
 

@@ -389,3 +389,33 @@ void orc_moe_token_ref(const uint16_t *X, const int *ids, const uint16_t *RW, co
     }
     free(h);
 }
+
+/* int2_moe/main.cpp:267-291 (the decode driver's check): o[n] = sum_j RW[g] * down(h),
+ * h = DT(silu(gate.x) * up.x) in double precision (up not rounded to DT) */
+void orc_moe_decode_token_ref(const uint16_t *X, const int *ids, const uint16_t *RW, const uint32_t *Bg,
+                              const uint16_t *Sg, const uint32_t *Bu, const uint16_t *Su,
+                              const uint32_t *Bd, const uint16_t *Sd, int t, int topk, int H, int I,
+                              double *o, int bf16) {
+    for (int n = 0; n < H; ++n) o[n] = 0.0;
+    float *h = (float *)malloc((size_t)I * sizeof(float));
+    for (int j = 0; j < topk; ++j) {
+        const int g = t * topk + j, e = ids[g];
+#pragma omp parallel for
+        for (int n = 0; n < I; ++n) {
+            double sg = 0.0, su = 0.0;
+            for (int k = 0; k < H; ++k) {
+                const double x = orc_tof(X[(size_t)t * H + k], bf16);
+                sg += x * proj_w(Bg, Sg, H, I, e, k, n, bf16);
+                su += x * proj_w(Bu, Su, H, I, e, k, n, bf16);
+            }
+            h[n] = orc_tof(orc_fromf((float)(sg / (1.0 + exp(-sg)) * su), bf16), bf16);
+        }
+#pragma omp parallel for
+        for (int n = 0; n < H; ++n) {
+            double s = 0.0;
+            for (int k = 0; k < I; ++k) s += h[k] * proj_w(Bd, Sd, I, H, e, k, n, bf16);
+            o[n] += s * orc_tof(RW[g], bf16);
+        }
+    }
+    free(h);
+}

@@ -67,6 +67,10 @@ void orc_moe_token_ref(const uint16_t *X, const int *ids, const uint16_t *RW, co
                        const uint16_t *Sg, const uint32_t *Bu, const uint16_t *Su,
                        const uint32_t *Bd, const uint16_t *Sd, int t, int topk, int H, int I,
                        double *o, int bf16);
+void orc_moe_decode_token_ref(const uint16_t *X, const int *ids, const uint16_t *RW, const uint32_t *Bg,
+                              const uint16_t *Sg, const uint32_t *Bu, const uint16_t *Su,
+                              const uint32_t *Bd, const uint16_t *Sd, int t, int topk, int H, int I,
+                              double *o, int bf16);
 
 #ifdef __cplusplus
 }

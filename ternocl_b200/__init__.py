@@ -273,3 +273,51 @@ def moe_combine(Y, inv, RW, T, topk, out=None, stream=None):
     call("ternocl_moe_combine", _ptr(Y), _ptr(inv), _ptr(RW), _ptr(O), int(T), N, int(topk), dtype_code(RW),
          _stream(stream))
     return O
+
+
+def moe_decode_gate_up(ids, X, Bg, Sg, Bu, Su, num_experts, topk, out=None, stream=None):
+    """H[g] = silu(X[g/topk] . gate_e) * (X[g/topk] . up_e), e = ids[g]; Bg/Bu [E, K/16, N]."""
+    torch = _torch()
+    _check_cuda(ids, X, Bg, Sg, Bu, Su, out)
+    G = ids.numel()
+    K = X.shape[1]
+    N = Sg.shape[-1]
+    H = torch.empty(G, N, dtype=X.dtype, device=X.device) if out is None else out
+    call("ternocl_moe_decode_gate_up", _ptr(ids), _ptr(X), _ptr(Bg), _ptr(Sg), _ptr(Bu), _ptr(Su), _ptr(H), G, N, K,
+         int(topk), int(num_experts), dtype_code(X), _stream(stream))
+    return H
+
+
+def moe_decode_down(ids, H, RW, B, S, num_experts, out=None, stream=None):
+    """Y[g] = RW[g] * (H[g] . down_e), e = ids[g]; fp32 [G, N]."""
+    torch = _torch()
+    _check_cuda(ids, H, RW, B, S, out)
+    G, K = H.shape
+    N = S.shape[-1]
+    Y = torch.empty(G, N, dtype=torch.float32, device=H.device) if out is None else out
+    call("ternocl_moe_decode_down", _ptr(ids), _ptr(H), _ptr(RW), _ptr(B), _ptr(S), _ptr(Y), G, N, K,
+         int(num_experts), dtype_code(H), _stream(stream))
+    return Y
+
+
+def moe_decode_reduce(Y, T, topk, dtype, out=None, stream=None):
+    """O[t] = sum_j Y[t*topk + j] (j ascending), in fp16/bf16 (dtype: a torch dtype)."""
+    torch = _torch()
+    _check_cuda(Y, out)
+    N = Y.shape[1]
+    O = torch.empty(T, N, dtype=dtype, device=Y.device) if out is None else out
+    call("ternocl_moe_decode_reduce", _ptr(Y), _ptr(O), int(T), N, int(topk), dtype_code(O), _stream(stream))
+    return O
+
+
+def moe_decode_down_sum(ids, H, RW, B, S, num_experts, topk, out=None, stream=None):
+    """O[t] = sum_j RW[g] * (H[g] . down_e), g = t*topk + j, e = ids[g]."""
+    torch = _torch()
+    _check_cuda(ids, H, RW, B, S, out)
+    G, K = H.shape
+    T = G // int(topk)
+    N = S.shape[-1]
+    O = torch.empty(T, N, dtype=H.dtype, device=H.device) if out is None else out
+    call("ternocl_moe_decode_down_sum", _ptr(ids), _ptr(H), _ptr(RW), _ptr(B), _ptr(S), _ptr(O), T, N, K, int(topk),
+         int(num_experts), dtype_code(H), _stream(stream))
+    return O

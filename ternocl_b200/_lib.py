@@ -46,6 +46,10 @@ SIGNATURES = {
     "ternocl_moe_gather": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "ternocl_moe_gemm": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp]),
     "ternocl_moe_combine": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+    "ternocl_moe_decode_gate_up": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
+    "ternocl_moe_decode_down": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "ternocl_moe_decode_reduce": (i32, [vp, vp, i32, i32, i32, i32, vp]),
+    "ternocl_moe_decode_down_sum": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
     "ternocl_bitcos_random": (sz, [i32, i32, f64, u64, vp, sz]),
     "ternocl_bitcos_pack": (sz, [vp, i32, i32, vp, sz]),
     "ternocl_bitcos_slice_ranks": (i32, [vp, i32, i32, i32, vp]),

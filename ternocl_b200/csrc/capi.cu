@@ -327,6 +327,8 @@ int ternocl_device_error(int reset) {
     v |= t;
     if (read_device_error_gemv_p(&t, reset) != cudaSuccess) return -1;
     v |= t;
+    if (read_device_error_moe_decode(&t, reset) != cudaSuccess) return -1;
+    v |= t;
     return (int)v;
 }
 
@@ -509,6 +511,61 @@ int ternocl_moe_combine(const float *Y, const int32_t *inv, const void *RW, void
     if (T == 0) return TERNOCL_OK;
     if (!Y || !inv || !RW || !O || !aligned(Y, 16) || !aligned(O, 8)) return TERNOCL_ERR_ARG;
     return cuda_status(moe_combine_launch(Y, inv, RW, O, T, N, topk, dtype, (cudaStream_t)stream));
+}
+
+// ---- MoE decode (int2_moe/int2_moe.cl:63-174) ----
+static int check_moe_decode(int dtype, int rows, int N, int K, int topk, int E) {
+    if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
+    if (rows < 0 || N <= 0 || K <= 0 || N % 16 || K % kGS || topk < 1 || E < 1) return TERNOCL_ERR_SHAPE;
+    return TERNOCL_OK;
+}
+
+int ternocl_moe_decode_gate_up(const int32_t *ids, const void *X, const uint32_t *Bg, const void *Sg,
+                               const uint32_t *Bu, const void *Su, void *H, int G, int N, int K, int topk,
+                               int num_experts, int dtype, void *stream) {
+    int st = check_moe_decode(dtype, G, N, K, topk, num_experts);
+    if (st != TERNOCL_OK) return st;
+    if (G % topk) return TERNOCL_ERR_SHAPE;
+    if (G == 0) return TERNOCL_OK;
+    if (!ids || !X || !Bg || !Sg || !Bu || !Su || !H) return TERNOCL_ERR_ARG;
+    if (!aligned(X, 16) || !aligned(Bg, 16) || !aligned(Bu, 16) || !aligned(Sg, 16) || !aligned(Su, 16))
+        return TERNOCL_ERR_ARG;
+    if (moe_decode_smem(K / kGS, topk, 0) > 227 * 1024) return TERNOCL_ERR_SHAPE;
+    return cuda_status(moe_decode_gate_up_launch(ids, X, Bg, Sg, Bu, Su, H, G, N, K, topk, num_experts, dtype,
+                                                 (cudaStream_t)stream));
+}
+
+int ternocl_moe_decode_down(const int32_t *ids, const void *H, const void *RW, const uint32_t *B, const void *S,
+                            float *Y, int G, int N, int K, int num_experts, int dtype, void *stream) {
+    int st = check_moe_decode(dtype, G, N, K, 1, num_experts);
+    if (st != TERNOCL_OK) return st;
+    if (G == 0) return TERNOCL_OK;
+    if (!ids || !H || !RW || !B || !S || !Y) return TERNOCL_ERR_ARG;
+    if (!aligned(H, 16) || !aligned(B, 16) || !aligned(S, 16)) return TERNOCL_ERR_ARG;
+    if (moe_decode_smem(K / kGS, 1, 1) > 227 * 1024) return TERNOCL_ERR_SHAPE;
+    return cuda_status(moe_decode_down_launch(ids, H, RW, B, S, Y, G, N, K, num_experts, dtype,
+                                              (cudaStream_t)stream));
+}
+
+int ternocl_moe_decode_reduce(const float *Y, void *O, int T, int N, int topk, int dtype, void *stream) {
+    if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
+    if (T < 0 || N <= 0 || N % 4 || topk < 1) return TERNOCL_ERR_SHAPE;
+    if (T == 0) return TERNOCL_OK;
+    if (!Y || !O || !aligned(Y, 16) || !aligned(O, 8)) return TERNOCL_ERR_ARG;
+    return cuda_status(moe_decode_reduce_launch(Y, O, T, N, topk, dtype, (cudaStream_t)stream));
+}
+
+int ternocl_moe_decode_down_sum(const int32_t *ids, const void *H, const void *RW, const uint32_t *B,
+                                const void *S, void *O, int T, int N, int K, int topk, int num_experts, int dtype,
+                                void *stream) {
+    int st = check_moe_decode(dtype, T, N, K, topk, num_experts);
+    if (st != TERNOCL_OK) return st;
+    if (T == 0) return TERNOCL_OK;
+    if (!ids || !H || !RW || !B || !S || !O) return TERNOCL_ERR_ARG;
+    if (!aligned(H, 16) || !aligned(B, 16) || !aligned(S, 16)) return TERNOCL_ERR_ARG;
+    if (moe_decode_smem(K / kGS, topk, 2) > 227 * 1024) return TERNOCL_ERR_SHAPE;
+    return cuda_status(moe_decode_down_sum_launch(ids, H, RW, B, S, O, T, N, K, topk, num_experts, dtype,
+                                                  (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -40,6 +40,7 @@
 // four classes.  The split-K reduction and the epilogue are gemv::finish.
 #include <cuda_runtime.h>
 
+#include "digit_common.cuh"
 #include "gemv_common.cuh"
 #include "launch.h"
 
@@ -53,8 +54,6 @@ constexpr int kWordBytes = 8 * kRowBytes;        // a group's words (1 KB)
 constexpr int kScaleBytes = kCols * 2;
 constexpr int kStageBytes = kWordBytes + kScaleBytes;  // per warp
 constexpr int kRingBytes = gemv::kStages * kStageBytes;
-constexpr uint32_t kMagicBits = 0x4B400000u;     // 1.5 * 2^23
-constexpr float kMagic = 12582912.0f;
 constexpr int kMaxRows = 4;                      // activation rows per CTA (13 n-columns)
 
 __host__ __device__ constexpr int nmma_for(int rows) { return (1 + 3 * rows + 7) / 8; }
@@ -72,22 +71,10 @@ struct I2DCols {
     __device__ static int thread_col(int g, int i) { return 4 * g + i; }
 };
 
-__device__ __forceinline__ uint32_t cls(uint32_t x, int j) {
-    return j == 3 ? (x & 0xC0C0C0C0u) : ((x << (6 - 2 * j)) & 0xC0C0C0C0u);
-}
-
-__device__ __forceinline__ void imma(int32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                     uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-template <class DT>
-__device__ __forceinline__ float to_f(uint16_t h) {
-    return DT::tof(h);
-}
+using digit::cls;
+using digit::imma;
+using digit::kMagic;
+using digit::kMagicBits;
 
 template <int W, int NMMA, class DT, int POSTOP, bool OUT_F32>
 __global__ void __launch_bounds__(W * 32) gemv_i2d_kernel(const gemv::Params p) {
@@ -148,49 +135,24 @@ __global__ void __launch_bounds__(W * 32) gemv_i2d_kernel(const gemv::Params p) 
     const int k0 = wg0 * kGS, klen = nwg * kGS;
     for (int m = 0; m < rows; ++m) {
         const uint16_t *arow = p.A + (size_t)(mb + m) * p.K + k0;
-        // row maximum of |A| (as magnitude bits; fp16 and bf16 order like their values)
+        // row maximum of |A| over the warp's range -> fixed-point exponent
         uint32_t mx = 0;
         for (int u = lane; u < klen / 8; u += 32) {
             const uint4 v = __ldg(reinterpret_cast<const uint4 *>(arow) + u);
-            // per half-word maxima (a plain 32-bit max would drop the low half)
-            mx = __vmaxu2(mx, __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
-                                       __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu)));
+            const uint32_t h2[8] = {v.x, v.y, v.z, v.w, 0u, 0u, 0u, 0u};
+            mx = max(mx, digit::absmax_bits(h2));
         }
-        mx = max(mx & 0xFFFFu, mx >> 16);
         mx = __reduce_max_sync(0xffffffffu, mx);
-        const float amax = to_f<DT>((uint16_t)mx);
-        const bool bad = DT::kBF16 ? mx >= 0x7F80u : mx >= 0x7C00u;  // Inf / NaN
-        int e = 0;
-        if (amax > 0.0f) {
-            int E;
-            frexpf(amax, &E);  // amax = f * 2^E, f in [0.5, 1)
-            e = min(max(22 - E, -126), 120);
-        }
-        const float up = __int_as_float((127 + e) << 23);            // 2^e
-        if (lane == 0) rscale[m] = bad ? __int_as_float(0x7FC00000) : __int_as_float((127 - e - 6) << 23);  // 2^-e / 64
+        const int e = digit::exponent_for<DT>(mx);
+        if (lane == 0) rscale[m] = digit::inverse_scale<DT>(mx, e);
         // digits: one word row (16 activations) per lane iteration
         char *pl0 = planes + (size_t)(3 * m) * pstride;
         for (int w = lane; w < klen / 16; w += 32) {
             const uint4 lo = __ldg(reinterpret_cast<const uint4 *>(arow + 16 * w));
             const uint4 hi = __ldg(reinterpret_cast<const uint4 *>(arow + 16 * w + 8));
             const uint32_t h2[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-            uint32_t x[16];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                x[2 * i] = __float_as_uint(fmaf(to_f<DT>((uint16_t)(h2[i] & 0xFFFFu)), up, kMagic));
-                x[2 * i + 1] = __float_as_uint(fmaf(to_f<DT>((uint16_t)(h2[i] >> 16)), up, kMagic));
-            }
             uint32_t d0[4], d1[4], d2[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {  // class j: rows j, j+4, j+8, j+12 of the word row
-                const uint32_t p01 = __byte_perm(x[j], x[j + 4], 0x5140);
-                const uint32_t p23 = __byte_perm(x[j + 8], x[j + 12], 0x5140);
-                d0[j] = __byte_perm(p01, p23, 0x5410);
-                d1[j] = __byte_perm(p01, p23, 0x7632);
-                const uint32_t q01 = __byte_perm(x[j], x[j + 4], 0x7362);
-                const uint32_t q23 = __byte_perm(x[j + 8], x[j + 12], 0x7362);
-                d2[j] = __byte_perm(q01, q23, 0x5410);
-            }
+            digit::word_digits<DT>(h2, e, d0, d1, d2);
             *reinterpret_cast<uint4 *>(pl0 + 16 * w) = make_uint4(d0[0], d0[1], d0[2], d0[3]);
             *reinterpret_cast<uint4 *>(pl0 + pstride + 16 * w) = make_uint4(d1[0], d1[1], d1[2], d1[3]);
             *reinterpret_cast<uint4 *>(pl0 + 2 * pstride + 16 * w) = make_uint4(d2[0], d2[1], d2[2], d2[3]);

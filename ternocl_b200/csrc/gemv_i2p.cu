@@ -32,6 +32,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "digit_common.cuh"
 #include "launch.h"
 #include "tc_common.cuh"
 
@@ -49,8 +50,6 @@ constexpr int kScaleBytes = kGroupsPerStage * kTileCols * 2;
 constexpr int kStageBytes = kConsumers * kSliceBytes + kScaleBytes;  // 17 KB
 constexpr int kStages = 4;
 constexpr int kPlaneBytes = kGroupsPerStage * 8 * 16;  // one digit plane of a stage
-constexpr uint32_t kMagicBits = 0x4B400000u;           // 1.5 * 2^23
-constexpr float kMagic = 12582912.0f;
 
 // shared memory map (from a 1024-byte aligned base)
 constexpr int kPlaneBufs = 3;                              // digits of stages i, i+1 (and i-1 in flight)
@@ -72,17 +71,10 @@ struct PParams {
     unsigned *ws_cnt;    // [tiles]
 };
 
-__device__ __forceinline__ uint32_t cls(uint32_t x, int j) {
-    return j == 3 ? (x & 0xC0C0C0C0u) : ((x << (6 - 2 * j)) & 0xC0C0C0C0u);
-}
-
-__device__ __forceinline__ void imma(int32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                     uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
+using digit::cls;
+using digit::imma;
+using digit::kMagic;
+using digit::kMagicBits;
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers * 32) : "memory"); }
 
@@ -230,49 +222,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_i2p_kernel(const PP
         const int gi = stg * kGroupsPerStage + w;
         const bool valid = gi < p.G;
         const uint32_t h2[8] = {r[0].x, r[0].y, r[0].z, r[0].w, r[1].x, r[1].y, r[1].z, r[1].w};
-        uint32_t mx = 0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx = __vmaxu2(mx, h2[k] & 0x7FFF7FFFu);
-        mx = max(mx & 0xFFFFu, mx >> 16);
+        uint32_t mx = digit::absmax_bits(h2);
         mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        const float amax = DT::tof((uint16_t)mx);
-        const bool bad = DT::kBF16 ? mx >= 0x7F80u : mx >= 0x7C00u;
-        int e = 0;
-        if (amax > 0.0f) {
-            int E;
-            frexpf(amax, &E);  // amax = f * 2^E, f in [0.5, 1)
-            e = min(max(22 - E, -126), 120);
-        }
+        const int e = digit::exponent_for<DT>(mx);
         if (lane < 8) {
-            const float up = __int_as_float((127 + e) << 23);  // 2^e
-            uint32_t x[16];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                x[2 * k] = __float_as_uint(fmaf(DT::tof((uint16_t)(h2[k] & 0xFFFFu)), up, kMagic));
-                x[2 * k + 1] = __float_as_uint(fmaf(DT::tof((uint16_t)(h2[k] >> 16)), up, kMagic));
-            }
             uint32_t d0[4], d1[4], d2[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {  // class j: rows j, j+4, j+8, j+12 of the word row
-                const uint32_t p01 = __byte_perm(x[j], x[j + 4], 0x5140);
-                const uint32_t p23 = __byte_perm(x[j + 8], x[j + 12], 0x5140);
-                d0[j] = __byte_perm(p01, p23, 0x5410);
-                d1[j] = __byte_perm(p01, p23, 0x7632);
-                const uint32_t q01 = __byte_perm(x[j], x[j + 4], 0x7362);
-                const uint32_t q23 = __byte_perm(x[j + 8], x[j + 12], 0x7362);
-                d2[j] = __byte_perm(q01, q23, 0x5410);
-            }
+            digit::word_digits<DT>(h2, e, d0, d1, d2);
             char *dst = pl + (w * 8 + lane) * 16;
             *reinterpret_cast<uint4 *>(dst) = make_uint4(d0[0], d0[1], d0[2], d0[3]);
             *reinterpret_cast<uint4 *>(dst + kPlaneBytes) = make_uint4(d1[0], d1[1], d1[2], d1[3]);
             *reinterpret_cast<uint4 *>(dst + 2 * kPlaneBytes) = make_uint4(d2[0], d2[1], d2[2], d2[3]);
         }
         // 2^-e / 64 (weights are 64 x code), 0 past K, NaN for a non-finite group
-        if (lane == 0)
-            fac[pb * kGroupsPerStage + w] =
-                !valid ? 0.0f : bad ? __int_as_float(0x7FC00000) : __int_as_float((127 - e - 6) << 23);
+        if (lane == 0) fac[pb * kGroupsPerStage + w] = valid ? digit::inverse_scale<DT>(mx, e) : 0.0f;
     };
 
     int cur = -1;

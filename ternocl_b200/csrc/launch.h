@@ -179,6 +179,18 @@ cudaError_t moe_gather_launch(const void *X, const int *perm, void *Xs, int G, i
 cudaError_t moe_combine_launch(const float *Y, const int *inv, const void *RW, void *O, int T, int N, int topk,
                                int dtype, cudaStream_t st);
 cudaError_t read_device_error_moe(unsigned *out, int reset);
+// MoE decode GEMVs (moe_decode.cu)
+size_t moe_decode_smem(int G, int topk, int mode);
+cudaError_t moe_decode_gate_up_launch(const int *ids, const void *X, const uint32_t *Bg, const void *Sg,
+                                      const uint32_t *Bu, const void *Su, void *H, int G, int N, int K, int topk,
+                                      int E, int dtype, cudaStream_t st);
+cudaError_t moe_decode_down_launch(const int *ids, const void *H, const void *RW, const uint32_t *B, const void *S,
+                                   float *Y, int G, int N, int K, int E, int dtype, cudaStream_t st);
+cudaError_t moe_decode_down_sum_launch(const int *ids, const void *H, const void *RW, const uint32_t *B,
+                                       const void *S, void *O, int T, int N, int K, int topk, int E, int dtype,
+                                       cudaStream_t st);
+cudaError_t moe_decode_reduce_launch(const float *Y, void *O, int T, int N, int topk, int dtype, cudaStream_t st);
+cudaError_t read_device_error_moe_decode(unsigned *out, int reset);
 // M from which TERNOCL_ALGO_AUTO picks the GEMM (int2_fp16_upcvt/main.cpp:160)
 constexpr int kGemmMinM = 64;
 // split-K factor the register-decode GEMV's planner picks when a workspace exists

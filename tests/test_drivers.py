@@ -12,7 +12,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 BIN = os.path.join(ROOT, "ternocl_b200", "bin")
-DRIVERS = ["int2_fp16_upcvt", "int1_fp16_upcvt", "int2_int8", "bitcos_fp16_upcvt", "int2_moe_prefill"]
+DRIVERS = ["int2_fp16_upcvt", "int1_fp16_upcvt", "int2_int8", "bitcos_fp16_upcvt", "int2_moe_prefill", "int2_moe"]
 
 AVG_DEV = re.compile(r"^Avg dev   time: [0-9.]+ ms \([0-9.]+ GFLOPS, [0-9.]+ GiB/s", re.M)
 VALID = re.compile(r"^Validation summary: (\d+)/(\d+) sets PASSED$", re.M)
@@ -29,10 +29,11 @@ def drv(name, *args, timeout=600):
 
 @pytest.mark.parametrize("name", DRIVERS)
 def test_usage(name):
-    r = drv(name, "--help") if name != "int2_moe_prefill" else drv(name, "--bogus")
+    moe = name.startswith("int2_moe")
+    r = drv(name, "--help") if not moe else drv(name, "--bogus")
     text = r.stdout + r.stderr
     assert "--m" in text or "--t" in text
-    assert r.returncode == (0 if name != "int2_moe_prefill" else 1)
+    assert r.returncode == (0 if not moe else 1)
 
 
 @pytest.mark.parametrize("name", DRIVERS[:4])
@@ -82,3 +83,13 @@ def test_moe_prefill_check():
     assert r.returncode == 0, r.stderr
     assert re.search(r"^check \(2 tokens\): max_abs_err \S+ \(max \|ref\| \S+, rel \S+\) PASS$", r.stdout, re.M), r.stdout
     assert re.search(r"\| layer [0-9.]+ us, [0-9.]+ TFLOPS, x48 = [0-9.]+ ms$", r.stdout, re.M), r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fused", [False, True])
+def test_moe_decode_check(fused):
+    args = ["--t", 2, "--e", 16, "--topk", 4, "--h", 512, "--i", 256, "--sets", 2, "--iters", 2]
+    r = drv("int2_moe", *(args + (["--fused"] if fused else [])))
+    assert r.returncode == 0, r.stderr
+    assert re.search(r"^check: max_abs_err \S+ \(max \|ref\| \S+, rel \S+\) PASS$", r.stdout, re.M), r.stdout
+    assert re.search(r"\| layer [0-9.]+ us, [0-9.]+ GiB/s, x48 layers = [0-9.]+ ms$", r.stdout, re.M), r.stdout

@@ -251,6 +251,23 @@ int ternocl_moe_gather(const void *X, const int32_t *perm, void *Xs, int G, int 
 int ternocl_moe_gemm(const int32_t *meta, const void *A_all, const uint32_t *B_all,
                      const void *S_all, void *C_all, const void *Other_all, int G, int N, int K,
                      int num_experts, int dtype, int postop, int out_f32, void *stream);
+/* int8 variant (int2_moe/int2_moe_prefill_int8.cl), qmode 0: ternocl_int8_quant_a on the T
+ * token rows gives Xq [T, K] and SAt [K/128, LDSA(T)]; gather_q, replaces int2_moe_gather_q
+ * (int2_moe_prefill_int8.cl:74-75), moves them into expert order:
+ *   Xsq[p] = Xq[t], SA[g, p] = SAt[g, t], t = perm[p] / topk;  SA [K/128, LDSA(G)], G = T*topk. */
+int ternocl_moe_gather_q(const int8_t *Xq, const void *SAt, const int32_t *perm, int8_t *Xsq, void *SA, int T,
+                         int G, int K, int topk, void *stream);
+/* Grouped s8 x s2 GEMM, replaces int2_moe_gemm_mt_i8 (int2_moe_prefill_int8.cl:88-91): for
+ * the rows p of every expert e,
+ *   C[p, n] = epi( sum_g float(dot_g(Aq[p], B_e[:, n])) * (SB_e[g, n] * (1 / SA[g, p])) )
+ * (the ternocl_int2_int8 formula per expert).  Aq_all int8 [G, K], SA [K/128, LDSA(G)]
+ * (16-byte aligned), B_all [E, K/16, N], SB_all [E, K/128, N], Other_all [G, N] (POSTOP
+ * 1/2), no bias.  qmode must be 0 (A_all unused): the codes of the reference's in-GEMM
+ * quantisation (qmode 1) equal ternocl_int8_quant_a's, since a * SA is exact in fp32. */
+int ternocl_moe_gemm_i8(const int32_t *meta, const void *A_all, const int8_t *Aq_all, const void *SA,
+                        const uint32_t *B_all, const void *SB_all, void *C_all, const void *Other_all, int G,
+                        int N, int K, int num_experts, int dtype, int postop, int out_f32, int qmode,
+                        void *stream);
 /* Combine, replaces int2_moe_combine (int2_moe_prefill.cl:144-145):
  * O[t, n] = DT(sum_j RW[t*topk+j] * Y[inv[t*topk+j], n]),  Y fp32 [G, N]. */
 int ternocl_moe_combine(const float *Y, const int32_t *inv, const void *RW, void *O, int T, int N,

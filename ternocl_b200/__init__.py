@@ -264,6 +264,33 @@ def moe_gemm(meta, A, B_all, S_all, num_experts, postop=0, out_f32=False, other=
     return C
 
 
+def moe_gather_q(Xq, SAt, perm, topk, stream=None):
+    """int8 rows Xq [T, K] and scales SAt [K/128, LDSA(T)] -> expert order: (Xsq [G, K], SA [K/128, LDSA(G)])."""
+    torch = _torch()
+    _check_cuda(Xq, SAt, perm)
+    T, K = Xq.shape
+    G = perm.numel()
+    Xsq = torch.empty(G, K, dtype=torch.int8, device=Xq.device)
+    SA = torch.empty(K // 128, int8_ldsa(G), dtype=SAt.dtype, device=Xq.device)
+    call("ternocl_moe_gather_q", _ptr(Xq), _ptr(SAt), _ptr(perm), _ptr(Xsq), _ptr(SA), T, G, K, int(topk),
+         _stream(stream))
+    return Xsq, SA
+
+
+def moe_gemm_i8(meta, Aq, SA, B_all, SB_all, num_experts, postop=0, out_f32=False, other=None, out=None,
+                stream=None):
+    """Grouped s8 x s2 GEMM over the expert-sorted int8 rows Aq [G, K] with scales SA [K/128, LDSA(G)];
+    B_all int32 [E, K/16, N], SB_all [E, K/128, N] (fp16/bf16, the output type)."""
+    _check_cuda(meta, Aq, SA, B_all, SB_all, other, out)
+    G, K = Aq.shape
+    N = B_all.shape[-1]
+    C = _out(G, N, SB_all, out_f32, out)
+    call("ternocl_moe_gemm_i8", _ptr(meta), None, _ptr(Aq), _ptr(SA), _ptr(B_all), _ptr(SB_all), _ptr(C),
+         _ptr(other), G, N, K, int(num_experts), dtype_code(SB_all), int(postop), int(bool(out_f32)), 0,
+         _stream(stream))
+    return C
+
+
 def moe_combine(Y, inv, RW, T, topk, out=None, stream=None):
     """O[t] = sum_j RW[t*topk+j] * Y[inv[t*topk+j]]; Y fp32 [G, N], RW [G] fp16/bf16."""
     torch = _torch()

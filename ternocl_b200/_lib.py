@@ -45,6 +45,8 @@ SIGNATURES = {
     "ternocl_moe_route": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
     "ternocl_moe_gather": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "ternocl_moe_gemm": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp]),
+    "ternocl_moe_gather_q": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+    "ternocl_moe_gemm_i8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, vp]),
     "ternocl_moe_combine": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "ternocl_moe_decode_gate_up": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
     "ternocl_moe_decode_down": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),

@@ -452,9 +452,12 @@ int ternocl_int2_int8(const void *A, const int8_t *Aq, const void *SA, const uin
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.Aq = Aq; a.SA = SA; a.qmode = qmode;
     a.stream = (cudaStream_t)stream;
-    // the tensor-core GEMM reads the int8 codes (qmode 0); qmode 1 quantises inside the
-    // GEMV kernel, which also serves any M in 8-row blocks
-    if (qmode == 0 && (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM)))
+    // the tensor-core GEMM reads the int8 codes (qmode 0) and copies the scale rows in
+    // 16-byte units; qmode 1 quantises inside the GEMV kernel, which also serves any M in
+    // 8-row blocks
+    const bool sa16 = aligned(SA, 16);
+    if (algo == TERNOCL_ALGO_GEMM && qmode == 0 && !sa16) return TERNOCL_ERR_ARG;
+    if (qmode == 0 && sa16 && (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM)))
         return cuda_status(int8_gemm_tc_launch(a));
     // no workspace in this signature: split-K stays within one thread-block cluster
     const GemvPlan p = gemv_i8_plan(M, N, K, false);
@@ -502,6 +505,35 @@ int ternocl_moe_gemm(const int32_t *meta, const void *A_all, const uint32_t *B_a
     a.M = G; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.stream = (cudaStream_t)stream;
     return cuda_status(moe_gemm_tc_launch(a, meta, E));
+}
+
+int ternocl_moe_gather_q(const int8_t *Xq, const void *SAt, const int32_t *perm, int8_t *Xsq, void *SA, int T, int G,
+                         int K, int topk, void *stream) {
+    if (T < 0 || G < 0 || K <= 0 || K % kGS || topk < 1 || (long long)T * topk != G) return TERNOCL_ERR_SHAPE;
+    if (G == 0) return TERNOCL_OK;
+    if (!Xq || !SAt || !perm || !Xsq || !SA || !aligned(Xq, 16) || !aligned(Xsq, 16) || !aligned(SAt, 2) ||
+        !aligned(SA, 2))
+        return TERNOCL_ERR_ARG;
+    return cuda_status(moe_gather_q_launch(Xq, SAt, perm, Xsq, SA, T, G, K, topk, (cudaStream_t)stream));
+}
+
+int ternocl_moe_gemm_i8(const int32_t *meta, const void *A_all, const int8_t *Aq_all, const void *SA,
+                        const uint32_t *B_all, const void *SB_all, void *C_all, const void *Other_all, int G, int N,
+                        int K, int num_experts, int dtype, int postop, int out_f32, int qmode, void *stream) {
+    (void)A_all;  // qmode 0 reads the int8 rows only
+    if (qmode != 0) return TERNOCL_ERR_ARG;
+    int st = check_gemm_common(Aq_all, B_all, SB_all, C_all, Other_all, nullptr, G, N, K, dtype, postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (postop == 3) return TERNOCL_ERR_ARG;  // no bias in the MoE GEMM (int2_moe_prefill_int8.cl:93)
+    if (!meta || num_experts < 1 || num_experts > 1024) return TERNOCL_ERR_ARG;
+    if (!SA || !aligned(SA, 16)) return TERNOCL_ERR_ARG;  // the scale rows are copied in 16-byte units
+    if (G == 0) return TERNOCL_OK;
+    GemvArgs a;
+    a.B = B_all; a.S = SB_all; a.C = C_all; a.Other = Other_all; a.Bias = nullptr;
+    a.M = G; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.Aq = Aq_all; a.SA = SA; a.qmode = 0;
+    a.stream = (cudaStream_t)stream;
+    return cuda_status(int8_gemm_tc_launch(a, meta, num_experts));
 }
 
 int ternocl_moe_combine(const float *Y, const int32_t *inv, const void *RW, void *O, int T, int N, int topk,

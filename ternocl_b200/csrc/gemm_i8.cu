@@ -24,6 +24,13 @@
 //               epilogue store.
 // The int32 dots are exact (|dot| <= 128 * 128 * 2 < 2^22, converted to float exactly).
 // Every mbarrier wait is bounded (tc::mbar_wait).
+//
+// Grouped (MoE) mode, int2_moe_gemm_mt_i8 (int2_moe/int2_moe_prefill_int8.cl:73-172): with
+// `meta` set, blockIdx.y is a row tile of the expert found by binary search over meta's
+// tile offsets, B and SB are that expert's [E, ...] slices, rows run from its first row
+// (any offset) to the next expert's, and SA [K/128, LDSA(G)] is read at the tile's rows.
+// The SA copy starts at the 8-element boundary below the tile's first row (bulk copies
+// start on 16 bytes), so a stage holds BM + 8 scales.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -42,7 +49,7 @@ constexpr int kAStageBytes = BM * BK;  // int8 A: one 128-byte-swizzled box of 1
 constexpr int kDecLBO = 128, kDecSBO = BK / 16 * 128 + 16;            // 1040
 constexpr int kDecStageBytes = (BN / 8) * kDecSBO;                     // 16640
 constexpr int kPackStageBytes = (BK / 16) * BN * 4;                    // 4096
-constexpr int kSbBytes = BN * 2, kSaBytes = BM * 2;
+constexpr int kSbBytes = BN * 2, kSaBytes = (BM + 8) * 2 + 16;  // 16-byte multiple
 constexpr int kTmemCols = 2 * BN;
 
 struct Smem {
@@ -63,6 +70,9 @@ struct Params {
     const uint16_t *Other;
     const void *Bias;
     int M, N, K, ldsa;
+    // grouped mode: [E+1 row offsets | E+1 row-tile offsets] of the expert-sorted rows
+    const int *meta;
+    int E;
 };
 
 __device__ __forceinline__ void mma_ss_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -112,10 +122,31 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
     // 1024-byte aligned base (the 128-byte swizzle pattern is anchored at 1024 B)
     char *smem = smem_raw + ((1024u - (tc::smem_addr(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int n0 = blockIdx.x * BN;
     const int nk = p.K / BK;
     const int ncols = min(BN, p.N - n0);
-    const int nrows_sa = min(BM, p.ldsa - m0);  // SA columns this tile may read (ldsa % 32 == 0)
+    int m0 = blockIdx.y * BM, m_end = p.M;
+    const uint32_t *Bw = p.B;
+    const uint16_t *SBw = p.SB;
+    if (p.meta) {
+        pdl_wait();  // meta comes from the routing kernel
+        const int E = p.E, tile = blockIdx.y;
+        if (tile >= p.meta[2 * E + 1]) return;  // uniform over the CTA, before any barrier
+        int lo = 0, hi = E - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.meta[E + 1 + mid] <= tile) lo = mid;
+            else hi = mid - 1;
+        }
+        m0 = p.meta[lo] + (tile - p.meta[E + 1 + lo]) * BM;
+        m_end = p.meta[lo + 1];
+        Bw += (size_t)lo * (p.K / 16) * p.N;
+        SBw += (size_t)lo * (p.K / BK) * p.N;
+    }
+    // SA columns sa0 .. sa0 + nsa of each group row: sa0 on a 16-byte boundary, within the
+    // padded pitch (ldsa % 32 == 0, so nsa * 2 is a multiple of 16)
+    const int sa0 = m0 & ~7, sa_off = m0 - sa0;
+    const int nsa = min(BM + 8, p.ldsa - sa0);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars);
     uint64_t *load_empty = full + kStages;
     uint64_t *dec_full = load_empty + kStages;
@@ -148,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
     if (warp == 0) {
         if (lane == 0) {
             pdl_wait();
-            const uint32_t pack_bytes = (BK / 16) * ncols * 4, sb_bytes = ncols * 2, sa_bytes = nrows_sa * 2;
+            const uint32_t pack_bytes = (BK / 16) * ncols * 4, sb_bytes = ncols * 2, sa_bytes = nsa * 2;
             int issued = 0;
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % kStages;
@@ -158,9 +189,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
                 tc::tma_load_2d(a, &tmA, kb * BK, m0, &full[s]);
                 char *pk = smem + Smem::pack + s * kPackStageBytes;
                 for (int r = 0; r < BK / 16; ++r)
-                    tc::bulk_g2s(pk + r * (BN * 4), p.B + (size_t)(kb * (BK / 16) + r) * p.N + n0, ncols * 4, &full[s]);
-                tc::bulk_g2s(smem + Smem::sb + s * kSbBytes, p.SB + (size_t)kb * p.N + n0, sb_bytes, &full[s]);
-                tc::bulk_g2s(smem + Smem::sa + s * kSaBytes, p.SA + (size_t)kb * p.ldsa + m0, sa_bytes, &full[s]);
+                    tc::bulk_g2s(pk + r * (BN * 4), Bw + (size_t)(kb * (BK / 16) + r) * p.N + n0, ncols * 4, &full[s]);
+                tc::bulk_g2s(smem + Smem::sb + s * kSbBytes, SBw + (size_t)kb * p.N + n0, sb_bytes, &full[s]);
+                tc::bulk_g2s(smem + Smem::sa + s * kSaBytes, p.SA + (size_t)kb * p.ldsa + sa0, sa_bytes, &full[s]);
                 ++issued;
             }
             for (int kb = issued - kStages < 0 ? 0 : issued - kStages; kb < issued; ++kb)
@@ -222,8 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
             tc::fence_after_sync();
             // (float)dot * (SB * inv), inv = 1/SA: the gold's formula (main.cpp:115-117)
             const uint16_t *sbs = reinterpret_cast<const uint16_t *>(smem + Smem::sb + s * kSbBytes) + half * (BN / 2);
-            const float sa = row < nrows_sa ? DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sa + s * kSaBytes)[row])
-                                            : 0.0f;
+            const float sa = sa_off + row < nsa
+                                 ? DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sa + s * kSaBytes)[sa_off + row])
+                                 : 0.0f;
             const float inv = sa == 0.0f ? 0.0f : __frcp_rn(sa);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {  // two chunks of 32 columns keep the register count down
@@ -253,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&load_empty[s]);
         }
-        if (ok && m < p.M) {
+        if (ok && m < m_end) {
             const int col0 = half * (BN / 2);
 #pragma unroll
             for (int c = 0; c < BN / 2; c += 2)
@@ -272,8 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
 
 }  // namespace gemm8
 
-// Aq [M, K] int8 row-major, SA [K/128, ldsa]
-cudaError_t int8_gemm_tc_launch(const GemvArgs &a) {
+// Aq [M, K] int8 row-major, SA [K/128, ldsa]; grouped (meta != null): M = G rows sorted by
+// expert, B and SB [E, ...]
+cudaError_t int8_gemm_tc_launch(const GemvArgs &a, const int *meta, int E) {
     using namespace gemm8;
     CUtensorMap map;
     const cudaError_t me = tc::make_map_sw128(&map, a.Aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.M, a.K, BM);
@@ -289,12 +322,15 @@ cudaError_t int8_gemm_tc_launch(const GemvArgs &a) {
     p.N = a.N;
     p.K = a.K;
     p.ldsa = (a.M + 31) & ~31;
+    p.meta = meta;
+    p.E = meta ? E : 0;
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
         auto kern = gemm_i8_kernel<DT, decltype(po)::value, decltype(of)::value>;
         cudaError_t err = ensure_smem(kern, Smem::total);
         if (err != cudaSuccess) return err;
-        const dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
+        // grouped: every expert adds at most one partial row tile
+        const dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM + (meta ? E : 0));
         return launch_kernel(kern, grid, dim3(kThreads), (size_t)Smem::total, a.stream, p, map);
     });
 }

@@ -167,7 +167,7 @@ bool gemm_use_256_rows(int M, int N);
 cudaError_t bitcos_gemm_tc_launch(const GemvArgs &a);
 cudaError_t read_device_error_gemm_bitcos(unsigned *out, int reset);
 // s8 x s2 prefill GEMM (gemm_i8.cu): a.Aq int8 [M, K], a.SA [K/128, ldsa], a.S = SB
-cudaError_t int8_gemm_tc_launch(const GemvArgs &a);
+cudaError_t int8_gemm_tc_launch(const GemvArgs &a, const int *meta = nullptr, int E = 0);
 cudaError_t read_device_error_gemm_i8(unsigned *out, int reset);
 // grouped (MoE) int2 GEMM over the rows of meta's experts; a.M = G rows
 cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E);
@@ -176,6 +176,8 @@ size_t moe_route_smem(int E);
 cudaError_t moe_route_launch(const int *ids, int *meta, int *perm, int *inv, int G, int E, int rpt,
                              cudaStream_t st);
 cudaError_t moe_gather_launch(const void *X, const int *perm, void *Xs, int G, int K, int topk, cudaStream_t st);
+cudaError_t moe_gather_q_launch(const int8_t *Xq, const void *SAt, const int *perm, int8_t *Xsq, void *SA, int T,
+                                int G, int K, int topk, cudaStream_t st);
 cudaError_t moe_combine_launch(const float *Y, const int *inv, const void *RW, void *O, int T, int N, int topk,
                                int dtype, cudaStream_t st);
 cudaError_t read_device_error_moe(unsigned *out, int reset);

@@ -5,8 +5,11 @@
 //   gather   (int2_moe_gather, :63-70)  Xs[p] = X[perm[p] / topk]
 //   combine  (int2_moe_combine, :143-156) O[t, n] = DT(sum_j RW[g] * Y[inv[g], n]),
 //            g = t*topk + j, j in increasing order, fp32 sum
+//   gather_q (int2_moe_gather_q, int2_moe_prefill_int8.cl:73-84) the int8 variant: int8
+//            rows and their per-group activation scales into expert order
 //
-// The grouped GEMM itself is the tcgen05 GEMM in grouped mode (gemm_tc.cu).
+// The grouped GEMMs themselves are the tcgen05 GEMMs in grouped mode (gemm_tc.cu for
+// fp16/bf16 activations, gemm_i8.cu for int8 ones).
 //
 // Routing: the order of the rows inside an expert is ascending in g (the reference's
 // follows its local atomics), so it is deterministic.  Up to 1024 rows one CTA (like
@@ -177,6 +180,26 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const uint4 *__restrict
     pdl_launch_dependents();
 }
 
+// int8 rows and their activation scales into expert order (int2_moe_gather_q,
+// int2_moe/int2_moe_prefill_int8.cl:73-84): Xsq[p] = Xq[t], SA[g, p] = SAt[g, t] with
+// t = perm[p] / topk and the scale pitches LDSA(T), LDSA(G)
+__global__ void __launch_bounds__(256) moe_gather_q_kernel(const uint4 *__restrict__ Xq,
+                                                          const uint16_t *__restrict__ SAt,
+                                                          const int *__restrict__ perm, uint4 *__restrict__ Xsq,
+                                                          uint16_t *__restrict__ SA, int T, int G, int K, int topk) {
+    pdl_wait();
+    const int K16 = K / 16, ngroups = K / kGS;
+    const size_t ldt = (size_t)((T + 31) & ~31), ldg = (size_t)((G + 31) & ~31);
+    for (int p = blockIdx.x; p < G; p += gridDim.x) {
+        const int t = perm[p] / topk;
+        const uint4 *src = Xq + (size_t)t * K16;
+        uint4 *dst = Xsq + (size_t)p * K16;
+        for (int k = threadIdx.x; k < K16; k += blockDim.x) dst[k] = src[k];
+        for (int g = threadIdx.x; g < ngroups; g += blockDim.x) SA[g * ldg + p] = SAt[g * ldt + t];
+    }
+    pdl_launch_dependents();
+}
+
 // thread per (token t, 4 columns)
 template <class DT>
 __global__ void __launch_bounds__(256) moe_combine_kernel(const float *__restrict__ Y, const int *__restrict__ inv,
@@ -225,6 +248,13 @@ cudaError_t moe_gather_launch(const void *X, const int *perm, void *Xs, int G, i
     const int blocks = G < 148 * 16 ? G : 148 * 16;
     return launch_kernel(moe_gather_kernel, dim3(blocks), dim3(256), 0, st, (const uint4 *)X, perm, (uint4 *)Xs, G,
                          K / 8, topk);
+}
+
+cudaError_t moe_gather_q_launch(const int8_t *Xq, const void *SAt, const int *perm, int8_t *Xsq, void *SA, int T,
+                                int G, int K, int topk, cudaStream_t st) {
+    const int blocks = G < 148 * 16 ? G : 148 * 16;
+    return launch_kernel(moe_gather_q_kernel, dim3(blocks), dim3(256), 0, st, (const uint4 *)Xq,
+                         (const uint16_t *)SAt, perm, (uint4 *)Xsq, (uint16_t *)SA, T, G, K, topk);
 }
 
 cudaError_t moe_combine_launch(const float *Y, const int *inv, const void *RW, void *O, int T, int N, int topk,

@@ -64,6 +64,15 @@ def test_more_host_checks_without_gpu():
     assert L.ternocl_moe_route(p, p, p, p, 8, 0, 128, None) == 1
     assert L.ternocl_moe_gemm(p, p, p, p, p, None, 8, 48, 128, 4, 0, 3, 0, None) == 2
     assert L.ternocl_moe_combine(p, p, p, p, 2, 50, 8, 0, None) == 1
+    # int8 MoE: qmode 0 only, SA on 16 bytes, no bias; gather_q needs G = T * topk
+    assert L.ternocl_moe_gemm_i8(p, p, p, p, p, p, p, None, 8, 16, 128, 2, 0, 0, 0, 1, None) == 2
+    assert L.ternocl_moe_gemm_i8(p, None, p, ctypes.c_void_p(66), p, p, p, None, 8, 16, 128, 2, 0, 0, 0, 0,
+                                 None) == 2
+    assert L.ternocl_moe_gemm_i8(p, None, p, p, p, p, p, None, 8, 16, 128, 2, 0, 3, 0, 0, None) == 2
+    assert L.ternocl_moe_gather_q(p, p, p, p, p, 3, 7, 128, 2, None) == 1
+    # the dense int8 GEMM copies SA rows in 16-byte units: misaligned SA is refused there
+    assert L.ternocl_int2_int8(p, p, ctypes.c_void_p(66), p, p, p, None, None, 256, 48, 128, 0, 0, 0, 0, 2,
+                               None) == 2
 
 
 def test_options():

@@ -77,12 +77,20 @@ def test_distinct_sets_and_tile_flags():
 
 
 @pytest.mark.gpu
-def test_moe_prefill_check():
-    r = drv("int2_moe_prefill", "--t", 256, "--e", 16, "--topk", 4, "--h", 512, "--i", 256, "--sets", 2,
-            "--iters", 2, "--check", 2)
+@pytest.mark.parametrize("int8", [None, 0, 1])
+def test_moe_prefill_check(int8):
+    args = ["--t", 256, "--e", 16, "--topk", 4, "--h", 512, "--i", 256, "--sets", 2, "--iters", 2, "--check", 2]
+    r = drv("int2_moe_prefill", *(args + (["--int8", int8] if int8 is not None else [])))
     assert r.returncode == 0, r.stderr
     assert re.search(r"^check \(2 tokens\): max_abs_err \S+ \(max \|ref\| \S+, rel \S+\) PASS$", r.stdout, re.M), r.stdout
     assert re.search(r"\| layer [0-9.]+ us, [0-9.]+ TFLOPS, x48 = [0-9.]+ ms$", r.stdout, re.M), r.stdout
+    if int8 is not None:
+        assert "int8 activations, qmode %d" % int8 in r.stdout
+        assert re.search(r"quant_x [0-9.]+ us .*quant_h [0-9.]+ us", r.stdout), r.stdout
+
+
+def test_moe_prefill_int8_flag_errors():
+    assert drv("int2_moe_prefill", "--int8", "2").returncode == 1
 
 
 @pytest.mark.gpu

@@ -7,23 +7,31 @@
 // with the int8 activations Aq and scales SA of ternocl_int8_quant_a (host gold:
 // compute_gold, int2_via_int2_x_int8_dpas/main.cpp:94-121).
 //
-// CTA tile 128 (M) x 128 (N); one stage = one 128-row group (K = 128).  448 threads:
+// CTA tile 128 (M) x 128 (N); one stage = one 128-row group (K = 128).  704 threads:
 //   warp 0      producer: Aq [128 x 128] through a 2-D tensor map (one box of 128 rows x
 //               128 bytes in the 128-byte swizzle layout), the group's 8 packed word rows, the SB row
-//               and the tile's SA entries through 1-D bulk copies (3 stages);
-//   warp 1      TMEM (2 x 128 int32 columns) and the MMA issuer: per group four
+//               and the tile's SA entries through 1-D bulk copies (5 stages);
+//   warp 1      TMEM (4 x 128 int32 columns) and the MMA issuer: per group four
 //               tcgen05.mma.cta_group::1.kind::i8 (M=128, N=128, K=32, s8 x s8 -> s32)
-//               into accumulator buffer g % 2, started fresh each group;
-//   warps 2-5   decode: thread n turns the 8 words of column n into 8 core-matrix rows of
-//               the K-major int8 B tile (2-bit two's complement = code_to_value, main.cpp:77;
-//               16 bytes in row order per word);
-//   warps 6-13  promotion: after each group, tcgen05.ld of the int32 accumulator (warp w
-//               owns TMEM lanes 32(w%4).., half the columns), then
+//               into accumulator buffer g % 4;
+//   warps 2-5   decode (4 stages ahead of the MMA): thread n turns the 8 words of column n
+//               into 8 core-matrix rows of the K-major int8 B tile, 64 x the code value (code_to_value, main.cpp:77):
+//               one shift-and-mask per four rows leaves each code in the top two bits of
+//               a byte, then a 4x4 byte transpose puts the 16 rows of the word in order;
+//               and the group's SB row (fp32) and 1/SA of the tile's rows into a ring of
+//               its own, so that a load stage is free as soon as it is decoded;
+//   warps 6-21  promotion: after each group, tcgen05.ld of the int32 accumulator (warp w
+//               owns TMEM lanes 32(w%4).. and 32 of the columns), then
 //               acc += float(dot) * (SB[g,n] * (1/SA[g,m])) in registers (the gold's
-//               formula; 1/SA is the IEEE quotient); after the last group, the fused
-//               epilogue store.
-// The int32 dots are exact (|dot| <= 128 * 128 * 2 < 2^22, converted to float exactly).
-// Every mbarrier wait is bounded (tc::mbar_wait).
+//               formula; 1/SA is the IEEE quotient) on packed f32x2 arithmetic, and the
+//               buffer's columns are set back to the bit pattern of 1.5 * 2^23 for its
+//               next group.
+// The accumulator buffers start every group at 0x4B400000 (1.5 * 2^23 as fp32), so after
+// the group's MMAs they hold the bits of the fp32 1.5 * 2^23 + 64 * dot (|64 * dot| <=
+// 64 * 128 * 127 * 2 < 2^22): one f32 subtraction gives 64 * dot exactly, and the 1/64 is
+// folded into 1/SA (a power of two: the products are the gold's, bit for bit).  After the
+// last group, the fused epilogue, each warp's 32 x 32 block turned through shared memory so
+// that a warp stores along rows.  Every mbarrier wait is bounded (tc::mbar_wait).
 //
 // Grouped (MoE) mode, int2_moe_gemm_mt_i8 (int2_moe/int2_moe_prefill_int8.cl:73-172): with
 // `meta` set, blockIdx.y is a row tile of the expert found by binary search over meta's
@@ -35,6 +43,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "digit_common.cuh"
 #include "launch.h"
 #include "tc_common.cuh"
 
@@ -42,15 +51,17 @@ namespace ternocl {
 namespace gemm8 {
 
 constexpr int BM = 128, BN = 128, BK = 128;
-constexpr int kStages = 3, kDecStages = 2;
-constexpr int kDecWarps = 4, kEpiWarps = 8;
+constexpr int kStages = 5, kDecStages = 4, kSclStages = 8;
+constexpr int kDecWarps = 4, kEpiWarps = 16;
+constexpr int kEpiCols = BN * 4 / kEpiWarps;  // accumulator columns per promotion warp (32)
 constexpr int kThreads = (2 + kDecWarps + kEpiWarps) * 32;
 constexpr int kAStageBytes = BM * BK;  // int8 A: one 128-byte-swizzled box of 128 rows x 128 B
 constexpr int kDecLBO = 128, kDecSBO = BK / 16 * 128 + 16;            // 1040
 constexpr int kDecStageBytes = (BN / 8) * kDecSBO;                     // 16640
 constexpr int kPackStageBytes = (BK / 16) * BN * 4;                    // 4096
 constexpr int kSbBytes = BN * 2, kSaBytes = (BM + 8) * 2 + 16;  // 16-byte multiple
-constexpr int kTmemCols = 2 * BN;
+constexpr int kAccBufs = 4;  // accumulator buffers: the MMA runs up to 3 groups ahead of the promotion
+constexpr int kTmemCols = kAccBufs * BN;  // all 512 columns: one CTA per SM (704 threads x 80 registers)
 
 struct Smem {
     static constexpr int dec = 0;
@@ -58,9 +69,15 @@ struct Smem {
     static constexpr int pack = a + kStages * kAStageBytes;
     static constexpr int sb = pack + kStages * kPackStageBytes;
     static constexpr int sa = sb + kStages * kSbBytes;
-    static constexpr int bars = sa + kStages * kSaBytes;
+    // per group, written by the decode warps for the promotion warps: the SB row as fp32
+    // [BN] and 1/SA / 64 of the tile's rows [BM]
+    static constexpr int scl = sa + kStages * kSaBytes;
+    static constexpr int kSclBytes = (BN + BM) * 4;
+    static constexpr int bars = scl + kSclStages * kSclBytes;
     static constexpr int total = bars + 256 + 1024;  // + alignment slack
 };
+
+static_assert(kStages * kAStageBytes >= kEpiWarps * 32 * 33 * 4, "epilogue tiles reuse the A stages");
 
 struct Params {
     const uint32_t *B;
@@ -99,21 +116,47 @@ __device__ __forceinline__ void transpose4x4(const uint32_t in[4], uint32_t out[
     out[3] = __byte_perm(t1, t3, 0x7632);
 }
 
-// int2 word (16 rows of one column) -> 16 int8 codes in row order
-__device__ __forceinline__ uint4 s8_row(uint32_t x) {
+// int2 word (16 rows of one column) -> 16 int8 values 64 * code in row order
+__device__ __forceinline__ uint4 s8x64_row(uint32_t x) {
     uint32_t r[4], o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t t = (x >> (2 * j)) & 0x03030303u;  // byte i: code of row 4i + j
-        r[j] = t + (t & 0x02020202u) * 0x7Eu;             // sign-extend 2 -> 8 bits
-    }
-    transpose4x4(r, o);  // o[q] byte i: row 4q + i
+    for (int j = 0; j < 4; ++j) r[j] = digit::cls(x, j);  // byte i: 64 * code of row 4i + j
+    transpose4x4(r, o);                                   // o[q] byte i: row 4q + i
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// int32 -> fp32 for |d| < 2^22 in two full-rate instructions
-__device__ __forceinline__ float i2f_small(uint32_t d) {
-    return __int_as_float((int)(d + 0x4B400000u)) - 12582912.0f;
+// packed fp32 pairs (f32x2 arithmetic of sm_100)
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// ncols (a multiple of 8) columns of this warp's lane quadrant set to v (x8 stores: 8
+// registers carry v)
+__device__ __forceinline__ void tmem_fill(uint32_t taddr, uint32_t v, int ncols) {
+#pragma unroll
+    for (int c = 0; c < ncols; c += 8)
+        asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};\n" ::"r"(taddr + c),
+                     "r"(v));
 }
 
 template <class DT, int POSTOP, bool OUT_F32>
@@ -152,21 +195,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
     uint64_t *dec_full = load_empty + kStages;
     uint64_t *dec_empty = dec_full + kDecStages;
     uint64_t *acc_full = dec_empty + kDecStages;
-    uint64_t *acc_empty = acc_full + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint64_t *acc_empty = acc_full + kAccBufs;
+    uint64_t *scl_full = acc_empty + kAccBufs;
+    uint64_t *scl_empty = scl_full + kSclStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(scl_empty + kSclStages);
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&load_empty[s], 1 + kDecWarps + kEpiWarps);
+            tc::mbar_init(&load_empty[s], 1 + kDecWarps);  // the MMA (A) and the decode warps
         }
         for (int d = 0; d < kDecStages; ++d) {
             tc::mbar_init(&dec_full[d], kDecWarps);
             tc::mbar_init(&dec_empty[d], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kAccBufs; ++b) {
             tc::mbar_init(&acc_full[b], 1);
             tc::mbar_init(&acc_empty[b], kEpiWarps);
+        }
+        for (int r = 0; r < kSclStages; ++r) {
+            tc::mbar_init(&scl_full[r], kDecWarps);
+            tc::mbar_init(&scl_empty[r], kEpiWarps);
         }
         tc::fence_mbar_init();
     }
@@ -201,10 +250,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_i8(BM, BN);
             for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % kStages, d = kb % kDecStages, b = kb & 1;
+                const int s = kb % kStages, d = kb % kDecStages, b = kb % kAccBufs;
                 if (!tc::mbar_wait(&full[s], (kb / kStages) & 1)) break;
                 if (!tc::mbar_wait(&dec_full[d], (kb / kDecStages) & 1)) break;
-                if (kb >= 2 && !tc::mbar_wait(&acc_empty[b], ((kb >> 1) - 1) & 1)) break;
+                // phase 0 of acc_empty is the promotion warps' initial fill of the buffer
+                if (!tc::mbar_wait(&acc_empty[b], (kb / kAccBufs) & 1)) break;
                 tc::fence_after_sync();
                 const uint32_t a = tc::smem_addr(smem + Smem::a + s * kAStageBytes);
                 const uint32_t bb = tc::smem_addr(smem + Smem::dec + d * kDecStageBytes);
@@ -212,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
                 for (int kk = 0; kk < BK / 32; ++kk) {
                     const uint64_t ad = tc::sdesc_kmajor_sw128(a + kk * 32);
                     const uint64_t bd = tc::sdesc_kmajor_noswz(bb + kk * 2 * kDecLBO, kDecLBO, kDecSBO);
-                    mma_ss_i8(tmem + b * BN, ad, bd, idesc, kk != 0);
+                    mma_ss_i8(tmem + b * BN, ad, bd, idesc, 1);  // onto the 1.5 * 2^23 fill
                 }
                 tc::mma_commit(&load_empty[s]);
                 tc::mma_commit(&dec_empty[d]);
@@ -220,77 +270,105 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
             }
         }
     } else if (warp < 2 + kDecWarps) {
-        // decode: thread n = column n of the tile, 8 word rows of the stage
+        // decode: thread n = column n of the tile, 8 word rows of the stage; and row n's scale
         const int n = tid - 64;
         for (int kb = 0; kb < nk; ++kb) {
-            const int s = kb % kStages, d = kb % kDecStages;
+            const int s = kb % kStages, d = kb % kDecStages, r = kb % kSclStages;
             if (!tc::mbar_wait(&full[s], (kb / kStages) & 1)) break;
             if (kb >= kDecStages && !tc::mbar_wait(&dec_empty[d], ((kb / kDecStages) - 1) & 1)) break;
+            if (kb >= kSclStages && !tc::mbar_wait(&scl_empty[r], ((kb / kSclStages) - 1) & 1)) break;
             const uint32_t *pk = reinterpret_cast<const uint32_t *>(smem + Smem::pack + s * kPackStageBytes);
             char *dst = smem + Smem::dec + d * kDecStageBytes + (n >> 3) * kDecSBO + (n & 7) * 16;
 #pragma unroll
-            for (int kc = 0; kc < BK / 16; ++kc) *reinterpret_cast<uint4 *>(dst + kc * 128) = s8_row(pk[kc * BN + n]);
+            for (int kc = 0; kc < BK / 16; ++kc) *reinterpret_cast<uint4 *>(dst + kc * 128) = s8x64_row(pk[kc * BN + n]);
+            // the SB row as fp32 (columns past the matrix hold stale values; never stored) and
+            // row n's 1/SA (the IEEE quotient, as the gold) / 64 (exact: 64 * dot comes back)
+            float *scl = reinterpret_cast<float *>(smem + Smem::scl + r * Smem::kSclBytes);
+            scl[n] = DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sb + s * kSbBytes)[n]);
+            const float sa = sa_off + n < nsa
+                                 ? DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sa + s * kSaBytes)[sa_off + n])
+                                 : 0.0f;
+            scl[BN + n] = (sa == 0.0f ? 0.0f : __frcp_rn(sa)) * 0.015625f;
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
                 tc::mbar_arrive(&dec_full[d]);
+                tc::mbar_arrive(&scl_full[r]);
                 tc::mbar_arrive(&load_empty[s]);
             }
         }
     } else {
-        // promotion + epilogue: warp w owns TMEM lanes 32(w%4)..+31 and columns half*64..+63
+        // promotion + epilogue: warp w owns TMEM lanes 32(w%4)..+31 and kEpiCols columns
         const int ew = warp - 2 - kDecWarps;
-        const int quad = warp & 3, half = ew >> 2;
+        const int quad = warp & 3, col0 = (ew >> 2) * kEpiCols;
         const int row = 32 * quad + lane, m = m0 + row;
-        float acc[BN / 2];
+        const uint32_t tl = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)col0;
+        // every accumulator buffer starts at the 1.5 * 2^23 pattern (phase 0 of acc_empty)
 #pragma unroll
-        for (int i = 0; i < BN / 2; ++i) acc[i] = 0.0f;
+        for (int b = 0; b < kAccBufs; ++b)
+#pragma unroll
+            tmem_fill(tl + b * BN, digit::kMagicBits, kEpiCols);
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < kAccBufs; ++b) tc::mbar_arrive(&acc_empty[b]);
+        uint64_t acc[kEpiCols / 2];  // column pairs (2i, 2i + 1) of this warp's columns
+#pragma unroll
+        for (int i = 0; i < kEpiCols / 2; ++i) acc[i] = 0;
+        const uint64_t neg_magic = f2(-digit::kMagic, -digit::kMagic);
         bool ok = true;
         for (int kb = 0; kb < nk && ok; ++kb) {
-            const int s = kb % kStages, b = kb & 1;
-            ok = tc::mbar_wait(&acc_full[b], (kb >> 1) & 1) && tc::mbar_wait(&full[s], (kb / kStages) & 1);
+            const int r = kb % kSclStages, b = kb % kAccBufs;
+            ok = tc::mbar_wait(&acc_full[b], (kb / kAccBufs) & 1) && tc::mbar_wait(&scl_full[r], (kb / kSclStages) & 1);
             if (!ok) break;
             tc::fence_after_sync();
-            // (float)dot * (SB * inv), inv = 1/SA: the gold's formula (main.cpp:115-117)
-            const uint16_t *sbs = reinterpret_cast<const uint16_t *>(smem + Smem::sb + s * kSbBytes) + half * (BN / 2);
-            const float sa = sa_off + row < nsa
-                                 ? DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sa + s * kSaBytes)[sa_off + row])
-                                 : 0.0f;
-            const float inv = sa == 0.0f ? 0.0f : __frcp_rn(sa);
+            // (float)dot * (SB * inv), inv = 1/SA: the gold's formula (main.cpp:115-117), with
+            // 64 * dot from the accumulator and inv / 64 (exact)
+            const float *scl = reinterpret_cast<const float *>(smem + Smem::scl + r * Smem::kSclBytes);
+            const float *sbf = scl + col0;
+            const float inv = scl[BN + row];
+            const uint64_t inv2 = f2(inv, inv);
+            const uint32_t taddr = tl + b * BN;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {  // two chunks of 32 columns keep the register count down
-                uint32_t d[32];
-                const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(b * BN + half * (BN / 2) + 32 * h);
-                tc::tmem_ld_u32x16(taddr, &d[0]);
-                tc::tmem_ld_u32x16(taddr + 16, &d[16]);
+            for (int h = 0; h < kEpiCols; h += 16) {  // chunks of 16 columns
+                uint32_t d[16];
+                tc::tmem_ld_u32x16(taddr + h, &d[0]);
                 tc::tmem_wait_ld();
-                if (h == 1) {
-                    tc::fence_before_sync();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
-                }
 #pragma unroll
-                for (int c = 0; c < 32; c += 8) {
-                    const uint4 sv = *reinterpret_cast<const uint4 *>(sbs + 32 * h + c);
-                    const uint32_t w[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float s0 = DT::tof((uint16_t)(w[i] & 0xffffu)), s1 = DT::tof((uint16_t)(w[i] >> 16));
-                        float &a0 = acc[32 * h + c + 2 * i], &a1 = acc[32 * h + c + 2 * i + 1];
-                        a0 = fmaf(i2f_small(d[c + 2 * i]), s0 * inv, a0);
-                        a1 = fmaf(i2f_small(d[c + 2 * i + 1]), s1 * inv, a1);
-                    }
+                for (int c = 0; c < 16; c += 4) {
+                    const float4 sv = *reinterpret_cast<const float4 *>(sbf + h + c);
+                    const uint64_t s01 = f2_mul(f2(sv.x, sv.y), inv2), s23 = f2_mul(f2(sv.z, sv.w), inv2);
+                    const uint64_t x01 = f2_add(f2(__uint_as_float(d[c]), __uint_as_float(d[c + 1])), neg_magic);
+                    const uint64_t x23 = f2_add(f2(__uint_as_float(d[c + 2]), __uint_as_float(d[c + 3])), neg_magic);
+                    uint64_t &a01 = acc[(h + c) / 2], &a23 = acc[(h + c) / 2 + 1];
+                    a01 = f2_fma(x01, s01, a01);
+                    a23 = f2_fma(x23, s23, a23);
                 }
+                // the columns back to 1.5 * 2^23 for group kb + 2 (d is dead: its registers
+                // can carry the fill); then the buffer goes to the MMA warp
+                tmem_fill(taddr + h, digit::kMagicBits, 16);
             }
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&load_empty[s]);
+            if (lane == 0) {
+                tc::mbar_arrive(&acc_empty[b]);
+                tc::mbar_arrive(&scl_empty[r]);
+            }
         }
-        if (ok && m < m_end) {
-            const int col0 = half * (BN / 2);
+        if (ok) {
+            // through a 32 x 32 tile of this warp (the load stages are free: every MMA is
+            // done), so that the stores run along the rows: lane j = column col0 + j
+            float *t = reinterpret_cast<float *>(smem + Smem::a) + ew * (32 * 33);
 #pragma unroll
-            for (int c = 0; c < BN / 2; c += 2)
-                if (col0 + c < ncols)
-                    epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, n0 + col0 + c, acc[c], acc[c + 1]);
+            for (int c = 0; c < kEpiCols; c += 2) f2_split(acc[c / 2], t[lane * 33 + c], t[lane * 33 + c + 1]);
+            __syncwarp();
+            const int n = n0 + col0 + lane;
+            const int rows = min(32, m_end - (m0 + 32 * quad));
+            if (col0 + lane < ncols)
+                for (int rr = 0; rr < rows; ++rr)
+                    epi_store<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m0 + 32 * quad + rr, n, t[rr * 33 + lane]);
         }
         pdl_launch_dependents();
     }

@@ -232,6 +232,17 @@ int ternocl_bitcos_upcvt(const void *A, const uint32_t *B, const void *S, const 
 int ternocl_hadamard_fwht(const void *x, const int8_t *signs, void *y, int rows, int K, int hb,
                           int use_signs, int dtype, void *stream);
 
+/* Hadamard-transformed BITCOS GEMV: ternocl_hadamard_fwht of A (signs, use_signs, hb)
+ * followed by ternocl_bitcos_upcvt on the result, in one launch with the transform done
+ * while the GEMV stages its activation slice (no intermediate in global memory).  The
+ * transformed activations are bit-identical to ternocl_hadamard_fwht's; the GEMV splits
+ * K on hb boundaries.  hb in {256, 512, 1024}, K % hb == 0, signs 16-byte aligned.
+ * Runs the GEMV kernel for every M (8-row blocks). */
+int ternocl_bitcos_upcvt_hadamard(const void *A, const int8_t *signs, int use_signs, int hb, const uint32_t *B,
+                                  const void *S, const uint32_t *SR, int ls, void *C, const void *Other,
+                                  const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,
+                                  void *stream);
+
 /* ---------------------------------------------------------------------------------
  * int2 MoE prefill (int2_moe/int2_moe_prefill.cl).  G = T * topk routed rows.
  *

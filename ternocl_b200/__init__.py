@@ -180,6 +180,20 @@ def bitcos_upcvt(A, B, S, SR=None, ls=1, postop=0, out_f32=False, other=None, bi
     return C
 
 
+def bitcos_upcvt_hadamard(A, B, S, hb, signs=None, SR=None, ls=1, postop=0, out_f32=False, other=None, bias=None,
+                          out=None, stream=None):
+    """C = epi(H_hb(signs * A) / sqrt(hb) @ decode_bitcos(B) * S) in one launch: the transform of
+    hadamard_fwht done while the BITCOS GEMV stages its activations."""
+    _check_cuda(A, B, S, SR, signs, other, bias, out)
+    M, K = A.shape
+    N = S.shape[1]
+    C = _out(M, N, A, out_f32, out)
+    call("ternocl_bitcos_upcvt_hadamard", _ptr(A), _ptr(signs), int(signs is not None), int(hb), _ptr(B), _ptr(S),
+         _ptr(SR), int(ls), _ptr(C), _ptr(other), _ptr(bias), M, N, K, dtype_code(A), int(postop),
+         int(bool(out_f32)), _stream(stream))
+    return C
+
+
 def bitcos_random(K, N, z, seed):
     """Host BITCOS buffer (numpy uint32) of random ternary weights at zero density z."""
     import numpy as np

@@ -41,6 +41,8 @@ SIGNATURES = {
     "ternocl_int2_int8_group_dots": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "ternocl_bitcos_upcvt": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp]),
     "ternocl_hadamard_fwht": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "ternocl_bitcos_upcvt_hadamard": (i32, [vp, vp, i32, i32, vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32,
+                                            i32, vp]),
     "ternocl_moe_rows_per_tile": (i32, []),
     "ternocl_moe_route": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
     "ternocl_moe_gather": (i32, [vp, vp, vp, i32, i32, i32, vp]),

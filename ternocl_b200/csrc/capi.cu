@@ -120,9 +120,15 @@ static GemvPlan gemv_i1_plan(int M, int N, int K, bool allow_ws) {
 }
 
 // BITCOS GEMV (gemv_bitcos.cu): same CTA shape, whole K range staged per CTA
-static GemvPlan gemv_bitcos_plan(int M, int N, int K, bool allow_ws) {
-    return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
-                       [&](int sk) { return bitcos_gemv_smem(M, K, sk); });
+// (with the fused transform, K splits on HB boundaries: SK <= K / HB)
+static GemvPlan gemv_bitcos_plan(int M, int N, int K, bool allow_ws, int had_hb = 0) {
+    GemvPlan p = gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
+                             [&](int sk) { return bitcos_gemv_smem(M, K, sk, had_hb); });
+    if (had_hb && p.SK > K / had_hb) {
+        p.SK = K / had_hb;
+        p.cluster = p.SK > 1 && p.SK <= kMaxClusterSK;
+    }
+    return p;
 }
 
 // s8 x s2 GEMV (gemv_int8.cu): same CTA shape, int8 activation staging
@@ -410,6 +416,33 @@ int ternocl_bitcos_upcvt(const void *A, const uint32_t *B, const void *S, const 
     // no workspace in this signature: split-K stays within one thread-block cluster
     const GemvPlan p = gemv_bitcos_plan(M, N, K, false);
     if (bitcos_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
+    a.SK = p.SK;
+    a.cluster = p.cluster ? 1 : 0;
+    return cuda_status(bitcos_gemv_launch(a));
+}
+
+int ternocl_bitcos_upcvt_hadamard(const void *A, const int8_t *signs, int use_signs, int hb, const uint32_t *B,
+                                  const void *S, const uint32_t *SR, int ls, void *C, const void *Other,
+                                  const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,
+                                  void *stream) {
+    int st = check_gemm_common(A, B, S, C, Other, Bias, M, N, K, dtype, postop, out_f32);
+    if (st != TERNOCL_OK) return st;
+    if (ls < 1) return TERNOCL_ERR_ARG;
+    if (K % (64 * ls)) return TERNOCL_ERR_SHAPE;  // bitcos_fp16_upcvt/main.cpp:129
+    if (ls > 1 && !SR) return TERNOCL_ERR_ARG;
+    if (hb != 256 && hb != 512 && hb != 1024) return TERNOCL_ERR_SHAPE;  // one warp per block
+    if (K % hb) return TERNOCL_ERR_SHAPE;  // hadamard_fwht.cl:68-69
+    if (use_signs && (!signs || !aligned(signs, 16))) return TERNOCL_ERR_ARG;
+    if (M == 0) return TERNOCL_OK;
+    GemvArgs a;
+    a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
+    a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
+    a.SR = SR; a.ls = ls;
+    a.had_hb = hb;
+    a.had_signs = use_signs ? signs : nullptr;
+    a.stream = (cudaStream_t)stream;
+    const GemvPlan p = gemv_bitcos_plan(M, N, K, false, hb);
+    if (bitcos_gemv_smem(M, K, p.SK, hb) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
     a.SK = p.SK;
     a.cluster = p.cluster ? 1 : 0;
     return cuda_status(bitcos_gemv_launch(a));

@@ -301,13 +301,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
         // promotion + epilogue: warp w owns TMEM lanes 32(w%4)..+31 and kEpiCols columns
         const int ew = warp - 2 - kDecWarps;
         const int quad = warp & 3, col0 = (ew >> 2) * kEpiCols;
-        const int row = 32 * quad + lane, m = m0 + row;
+        const int row = 32 * quad + lane;
         const uint32_t tl = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)col0;
         // every accumulator buffer starts at the 1.5 * 2^23 pattern (phase 0 of acc_empty)
 #pragma unroll
-        for (int b = 0; b < kAccBufs; ++b)
-#pragma unroll
-            tmem_fill(tl + b * BN, digit::kMagicBits, kEpiCols);
+        for (int b = 0; b < kAccBufs; ++b) tmem_fill(tl + b * BN, digit::kMagicBits, kEpiCols);
         tc::tmem_wait_st();
         tc::fence_before_sync();
         __syncwarp();

@@ -21,7 +21,11 @@
 //   4. the sign words that cover [start rank, end rank] of each column (plus one word
 //      for the 64-bit window), which are contiguous in the stream;
 //   5. (after griddepcontrol.wait) the activation rows, 16-byte units swizzled so the
-//      main loop's reads are conflict-free.
+//      main loop's reads are conflict-free.  With the fused Hadamard transform (had_L > 0,
+//      the reference's hadamard_fwht -> BITCOS GEMV pipeline in one launch) each HB-wide
+//      block of the CTA's K range (K split on HB boundaries) is then sign-flipped and
+//      transformed in place by one warp, as hadamard_fwht does it (same fp32 stages in the
+//      same order, the same DT rounding): the result equals the two-kernel pipeline's.
 // Main loop (per warp, per group): lane (g, q) takes bitmap word q (rows 32q..32q+31)
 // of columns 4g..4g+3.  The four q lanes of a column scan their popcounts (packed
 // 4 columns x 8 bits, two shuffles) to get each word's rank, and funnel-shift a
@@ -35,6 +39,7 @@
 #include <cuda_runtime.h>
 
 #include "gemv_common.cuh"
+#include "hadamard_common.cuh"
 #include "launch.h"
 
 namespace ternocl {
@@ -56,9 +61,75 @@ struct BitcosCols {
 
 __host__ __device__ inline int sign_cap(int ng) { return 4 * ng + 3; }  // staged sign words per column
 
-__host__ __device__ inline size_t bitcos_smem_bytes(int rows, int ng) {
+__host__ __device__ inline size_t bitcos_smem_bytes(int rows, int ng, bool had = false) {
     return (size_t)kRedBytes + kMetaBytes + (size_t)ng * 32 * 2 + (size_t)ng * 4 * 32 * 4 +
-           (size_t)32 * sign_cap(ng) * 4 + (size_t)rows * ((size_t)ng * kGS * 2 + 16);
+           (size_t)32 * sign_cap(ng) * 4 + (size_t)rows * ((size_t)ng * kGS * 2 + 16) + (had ? (size_t)ng * kGS : 0);
+}
+
+// Sign flip + FWHT, in place, of HB = 32 E-wide blocks of the CTA's staged activation rows
+// [rows x krange] (the swizzled units of step 5; sgn = the range's signs, staged or null):
+// one warp per block, lane l holding elements E l .. E l + E - 1, the stages of stride
+// 1 .. E/2 in registers and those of stride E .. HB/2 across lanes (__shfl_xor), every
+// stage the fp32 pair (a + b, a - b), in increasing stride order as hadamard_fwht, then
+// the scale and the DT rounding of the standalone kernel.
+template <class DT, int E>
+__device__ void stage_fwht(const gemv::Params &p, char *act, int act_stride, const int8_t *sgn, int rows,
+                           int krange, int warp, int lane) {
+    constexpr int HB = 32 * E;
+    const int nb = krange / HB, total = rows * nb;
+    for (int blk = warp; blk < total; blk += gemv::kWarps) {
+        const int m = blk / nb, k0 = (blk % nb) * HB + lane * E;  // within the range
+        char *row = act + (size_t)m * act_stride;
+        float v[E];
+#pragma unroll
+        for (int q = 0; q < E / 8; ++q) {
+            const int u = k0 / 8 + q;
+            const uint4 w4 = *reinterpret_cast<const uint4 *>(row + (size_t)(u ^ (((u >> 3) & 1) << 1)) * 16);
+            const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[8 * q + 2 * j] = DT::tof((uint16_t)(w[j] & 0xffffu));
+                v[8 * q + 2 * j + 1] = DT::tof((uint16_t)(w[j] >> 16));
+            }
+        }
+        if (sgn) {
+#pragma unroll
+            for (int q = 0; q < E / 8; ++q) {  // 8 signs per 8-byte read
+                const uint2 sv = *reinterpret_cast<const uint2 *>(sgn + k0 + 8 * q);
+                const uint32_t sw[2] = {sv.x, sv.y};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[8 * q + j] *= (float)(int8_t)((sw[j >> 2] >> (8 * (j & 3))) & 0xffu);
+            }
+        }
+#pragma unroll
+        for (int h = 1; h < E; h <<= 1)
+#pragma unroll
+            for (int j = 0; j < E; ++j)
+                if ((j & h) == 0) {
+                    const float a = v[j], b = v[j + h];
+                    v[j] = a + b;
+                    v[j + h] = a - b;
+                }
+#pragma unroll
+        for (int c = 0; c < 5; ++c) {  // stride E << c: lane bit c
+            const bool upper = (lane >> c) & 1;
+#pragma unroll
+            for (int j = 0; j < E; ++j) {
+                const float o = __shfl_xor_sync(0xffffffffu, v[j], 1 << c);
+                v[j] = upper ? o - v[j] : v[j] + o;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < E / 8; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[j] = (uint32_t)DT::fromf(v[8 * q + 2 * j] * p.had_scale) |
+                       ((uint32_t)DT::fromf(v[8 * q + 2 * j + 1] * p.had_scale) << 16);
+            const int u = k0 / 8 + q;
+            *reinterpret_cast<uint4 *>(row + (size_t)(u ^ (((u >> 3) & 1) << 1)) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
 }
 
 template <class DT, int POSTOP, bool OUT_F32>
@@ -72,7 +143,9 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
     const int N = p.N, K = p.K;
     const int G = K / kGS;
     const int sk = blockIdx.y;
-    const int cg0 = (int)((long long)G * sk / p.SK), cg1 = (int)((long long)G * (sk + 1) / p.SK);
+    // K split in units of gran groups (the fused transform's blocks stay within one CTA)
+    const int gran = p.had_L ? (1 << p.had_L) / kGS : 1, U = G / gran;
+    const int cg0 = gran * (int)((long long)U * sk / p.SK), cg1 = gran * (int)((long long)U * (sk + 1) / p.SK);
     const int ng = cg1 - cg0;
     const int wg0 = cg0 + ng * warp / gemv::kWarps, wg1 = cg0 + ng * (warp + 1) / gemv::kWarps;
     const int rows = min(8, p.M - mb);
@@ -177,9 +250,20 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
         gemv::cp_async16(act + (size_t)m * act_stride + (size_t)pu * 16,
                          p.A + (size_t)(mb + m) * K + (size_t)cg0 * kGS + (size_t)u * 8);
     }
+    // the fused transform's signs of the range follow the rows
+    int8_t *sgn = reinterpret_cast<int8_t *>(act + (size_t)rows * act_stride);
+    if (p.had_L && p.had_signs)
+        for (int u = tid; u < krange / 16; u += kThreads) gemv::cp_async16(sgn + 16 * u, p.had_signs + cg0 * kGS + 16 * u);
     gemv::cp_async_commit();
     gemv::cp_async_wait<0>();
     __syncthreads();
+    if (p.had_L) {
+        const int8_t *sg = p.had_signs ? sgn : nullptr;
+        if (p.had_L == 8) stage_fwht<DT, 8>(p, act, act_stride, sg, rows, krange, warp, lane);
+        else if (p.had_L == 9) stage_fwht<DT, 16>(p, act, act_stride, sg, rows, krange, warp, lane);
+        else stage_fwht<DT, 32>(p, act, act_stride, sg, rows, krange, warp, lane);
+        __syncthreads();
+    }
 
     float acc[2][4];
 #pragma unroll
@@ -271,10 +355,10 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
 template <class DT, int POSTOP, bool OUT_F32>
 cudaError_t launch_t(const GemvArgs &a) {
     gemv::Params p = gemv::gemv_params_impl(a);
-    const int G = a.K / kGS;
-    const int max_ng = (G + a.SK - 1) / a.SK;
+    const int G = a.K / kGS, gran = a.had_hb ? a.had_hb / kGS : 1;
+    const int max_ng = gran * ((G / gran + a.SK - 1) / a.SK);
     const int rows = a.M < 8 ? a.M : 8;
-    const size_t smem = bitcos_smem_bytes(rows, max_ng);
+    const size_t smem = bitcos_smem_bytes(rows, max_ng, a.had_hb != 0);
     auto kern = bitcos_gemv_kernel<DT, POSTOP, OUT_F32>;
     if (smem > 48 * 1024) {
         cudaError_t e = ensure_smem(kern, smem);
@@ -286,9 +370,9 @@ cudaError_t launch_t(const GemvArgs &a) {
 
 }  // namespace
 
-size_t bitcos_gemv_smem(int M, int K, int SK) {
-    const int G = K / kGS;
-    return bitcos_smem_bytes(M < 8 ? M : 8, (G + SK - 1) / SK);
+size_t bitcos_gemv_smem(int M, int K, int SK, int had_hb) {
+    const int G = K / kGS, gran = had_hb ? had_hb / kGS : 1;
+    return bitcos_smem_bytes(M < 8 ? M : 8, gran * ((G / gran + SK - 1) / SK), had_hb != 0);
 }
 
 cudaError_t bitcos_gemv_launch(const GemvArgs &a) {

@@ -23,6 +23,7 @@
 // waiting) sums the SK partials in split order and resets the counter.  Either way
 // the summation order is fixed, so results are bitwise reproducible.
 #pragma once
+#include <cmath>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -47,6 +48,9 @@ struct Params {
     const uint16_t *S;
     const uint32_t *SR;  // BITCOS slice ranks [ls-1][N] (unused by the other layouts)
     int ls;
+    int had_L;               // BITCOS: log2 of the fused FWHT block (0: no transform)
+    const int8_t *had_signs;  // its sign vector [K] (null: no sign flip)
+    float had_scale;          // 1/sqrt(2^had_L), as the standalone transform
     void *C;
     const uint16_t *Other;
     const void *Bias;
@@ -103,6 +107,9 @@ inline Params gemv_params_impl(const GemvArgs &a) {
     p.S = (const uint16_t *)a.S;
     p.SR = a.SR;
     p.ls = a.ls;
+    p.had_L = a.had_hb ? 31 - __builtin_clz((unsigned)a.had_hb) : 0;
+    p.had_signs = a.had_signs;
+    p.had_scale = a.had_hb ? (float)(1.0 / std::sqrt((double)a.had_hb)) : 1.0f;
     p.C = a.C;
     p.Other = (const uint16_t *)a.Other;
     p.Bias = a.Bias;

@@ -23,6 +23,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "hadamard_common.cuh"
 #include "launch.h"
 
 namespace ternocl {
@@ -31,20 +32,8 @@ namespace {
 constexpr int kFwhtThreads = 256;
 constexpr int kFwhtElems = kFwhtThreads * 16;
 
-__device__ __forceinline__ int pad16(int i) { return i + (i >> 4); }
-
-// the four radix-2 stages over the bits of j, in increasing order
-__device__ __forceinline__ void wht16(float v[16]) {
-#pragma unroll
-    for (int h = 1; h < 16; h <<= 1)
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if ((j & h) == 0) {
-                const float a = v[j], b = v[j + h];
-                v[j] = a + b;
-                v[j + h] = a - b;
-            }
-}
+using fwht::pad16;
+using fwht::wht16;
 
 template <class DT, int L>
 __global__ void __launch_bounds__(kFwhtThreads) fwht_kernel(const uint16_t *x,  // may alias y

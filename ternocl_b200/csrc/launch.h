@@ -47,6 +47,10 @@ struct GemvArgs {
     // BITCOS: slice ranks [ls-1][N] of the reference's ls K slices
     const uint32_t *SR = nullptr;
     int ls = 1;
+    // BITCOS GEMV with the sign flip + FWHT of the activations fused into their staging
+    // (had_hb = 0: off); signs int8 [K] or null
+    int had_hb = 0;
+    const int8_t *had_signs = nullptr;
     // column-sharded GEMV (world > 0): see gemv::Params
     int world = 0, rank = 0, n_off = 0, N_out = 0;
     unsigned epoch = 0;
@@ -138,7 +142,7 @@ cudaError_t int1_gemv_launch(const GemvArgs &a);
 cudaError_t bitcos_gemv_launch(const GemvArgs &a);
 cudaError_t hadamard_launch(const void *x, const int8_t *signs, void *y, int rows, int K, int hb, int use_signs,
                             int dtype, cudaStream_t st);
-size_t bitcos_gemv_smem(int M, int K, int SK);
+size_t bitcos_gemv_smem(int M, int K, int SK, int had_hb = 0);
 size_t int1_gemv_smem(int M, int K, int SK);
 size_t int8_gemv_smem(int M, int K, int SK);
 cudaError_t int2_gemv_launch(const GemvArgs &a);

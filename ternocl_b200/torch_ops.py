@@ -10,6 +10,7 @@ operator without running it.  The activation may carry leading batch dimensions
 
   int2_linear / int1_linear   ternocl_int2_upcvt / ternocl_int1_upcvt
   bitcos_linear               ternocl_bitcos_upcvt
+  bitcos_hadamard_linear      ternocl_bitcos_upcvt_hadamard
   int8_linear                 ternocl_int8_quant_a + ternocl_int2_int8 (qmode 0)
   hadamard                    ternocl_hadamard_fwht
   moe_prefill                 route, gather (or quant + gather_q), up, gate (SiLU x up),
@@ -73,6 +74,22 @@ def bitcos_linear(A: torch.Tensor, B: torch.Tensor, S: torch.Tensor, SR: Optiona
 
 @bitcos_linear.register_fake
 def _(A, B, S, SR=None, ls=1, postop=0, out_f32=False, other=None, bias=None):
+    return _fake_linear(A, S.shape[1], out_f32)
+
+
+@torch.library.custom_op(_NS + "::bitcos_hadamard_linear", mutates_args=())
+def bitcos_hadamard_linear(A: torch.Tensor, B: torch.Tensor, S: torch.Tensor, hb: int,
+                           signs: Optional[torch.Tensor] = None, SR: Optional[torch.Tensor] = None, ls: int = 1,
+                           postop: int = 0, out_f32: bool = False, other: Optional[torch.Tensor] = None,
+                           bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bitcos_linear of the sign-flipped, blockwise Hadamard-transformed A, in one launch."""
+    C = tl.bitcos_upcvt_hadamard(_rows(A), B, S, hb, signs=signs, SR=SR, ls=ls, postop=postop, out_f32=out_f32,
+                                 other=None if other is None else _rows(other), bias=bias)
+    return C.reshape(*A.shape[:-1], S.shape[1])
+
+
+@bitcos_hadamard_linear.register_fake
+def _(A, B, S, hb, signs=None, SR=None, ls=1, postop=0, out_f32=False, other=None, bias=None):
     return _fake_linear(A, S.shape[1], out_f32)
 
 

@@ -70,6 +70,13 @@ def test_more_host_checks_without_gpu():
                                  None) == 2
     assert L.ternocl_moe_gemm_i8(p, None, p, p, p, p, p, None, 8, 16, 128, 2, 0, 3, 0, 0, None) == 2
     assert L.ternocl_moe_gather_q(p, p, p, p, p, 3, 7, 128, 2, None) == 1
+    # fused Hadamard + BITCOS GEMV: HB in 256..2048 dividing K, aligned signs
+    assert L.ternocl_bitcos_upcvt_hadamard(p, p, 1, 2048, p, p, None, 1, p, None, None, 1, 48, 4096, 0, 0, 0,
+                                           None) == 1
+    assert L.ternocl_bitcos_upcvt_hadamard(p, p, 1, 1024, p, p, None, 1, p, None, None, 1, 48, 5376, 0, 0, 0,
+                                           None) == 1
+    assert L.ternocl_bitcos_upcvt_hadamard(p, ctypes.c_void_p(72), 1, 256, p, p, None, 1, p, None, None, 1, 48,
+                                           5376, 0, 0, 0, None) == 2
     # the dense int8 GEMM copies SA rows in 16-byte units: misaligned SA is refused there
     assert L.ternocl_int2_int8(p, p, ctypes.c_void_p(66), p, p, p, None, None, 256, 48, 128, 0, 0, 0, 0, 2,
                                None) == 2

@@ -8,7 +8,8 @@ import torch
 
 import ternocl_b200.torch_ops  # noqa: F401  (registers torch.ops.ternocl)
 
-OPS = ["int2_linear", "int1_linear", "bitcos_linear", "int8_linear", "hadamard", "moe_prefill", "moe_decode"]
+OPS = ["int2_linear", "int1_linear", "bitcos_linear", "bitcos_hadamard_linear", "int8_linear", "hadamard",
+       "moe_prefill", "moe_decode"]
 
 
 def test_registered():

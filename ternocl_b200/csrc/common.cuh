@@ -100,6 +100,31 @@ __device__ __forceinline__ void epi_store2(void *__restrict__ C, const uint16_t 
     }
 }
 
+// A warp's 32 x 32 block of results, lane = row (v: 32 consecutive columns of its row, as
+// a TMEM lane holds them), stored along rows through the warp's shared tile t[32][33]
+// (conflict-free both ways): lanes 0-15 and 16-31 store column pairs of two rows at a
+// time, so a store instruction writes two contiguous row segments.  Rows from m_end on
+// and columns from ncols on (ncols even) are skipped.
+template <class DT, int POSTOP, bool OUT_F32>
+__device__ __forceinline__ void epi_store_rows32(float *t, const float (&v)[32], void *__restrict__ C,
+                                                 const uint16_t *__restrict__ other, const void *__restrict__ bias,
+                                                 int N, int mrow, int m_end, int n, int ncols, int lane) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[lane * 33 + j] = v[j];
+    __syncwarp();
+    const int rsub = lane >> 4, c2 = 2 * (lane & 15);
+    if (c2 < ncols) {
+#pragma unroll 4
+        for (int rr = 0; rr < 32; rr += 2) {
+            const int r = rr + rsub;
+            if (mrow + r < m_end)
+                epi_store2<DT, POSTOP, OUT_F32>(C, other, bias, N, mrow + r, n + c2, t[r * 33 + c2], t[r * 33 + c2 + 1]);
+        }
+    }
+    __syncwarp();
+}
+constexpr int kEpiTileBytes = 32 * 33 * 4;
+
 // ---------------------------------------------------------------------------------
 // int2 weight decode in registers.
 //

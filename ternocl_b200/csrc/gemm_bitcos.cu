@@ -270,20 +270,20 @@ __global__ void __launch_bounds__(kThreads, 1) bitcos_gemm_kernel(const Params p
         }
         if (tc::mbar_wait(acc_full, 0)) {
             tc::fence_after_sync();
+            // through a 32 x 32 tile per warp in the (now free) decode stages: stores along rows
             const int quad = warp & 3, half = (warp - 2) >> 2;
+            float *t = reinterpret_cast<float *>(smem + C::dec + (warp - 2) * kEpiTileBytes);
 #pragma unroll 1
-            for (int c = 0; c < HALVES * BN / 2 / 16; ++c) {
-                const int h = c / (BN / 2 / 16);
-                const int col = half * (BN / 2) + 16 * (c % (BN / 2 / 16));
-                const int m = m0 + h * BM + 32 * quad + lane;
-                float v[16];
-                tc::tmem_ld<16>(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(h * BN + col), v);
+            for (int c = 0; c < HALVES * BN / 2 / 32; ++c) {
+                const int h = c / (BN / 2 / 32);
+                const int col = half * (BN / 2) + 32 * (c % (BN / 2 / 32));
+                float v[32];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(h * BN + col);
+                tc::tmem_ld<16>(taddr, *reinterpret_cast<float(*)[16]>(&v[0]));
+                tc::tmem_ld<16>(taddr + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
                 tc::tmem_wait_ld();
-                if (m < p.M && col < ncols) {
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2)
-                        epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, n0 + col + i, v[i], v[i + 1]);
-                }
+                epi_store_rows32<DT, POSTOP, OUT_F32>(t, v, p.C, p.Other, p.Bias, p.N, m0 + h * BM + 32 * quad, p.M,
+                                                      n0 + col, ncols - col, lane);
             }
         }
         pdl_launch_dependents();

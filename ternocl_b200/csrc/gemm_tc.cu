@@ -191,7 +191,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
             if (p.meta[E + 1 + mid] <= tile) lo = mid;
             else hi = mid - 1;
         }
-        m0 = p.meta[lo] + (tile - p.meta[E + 1 + lo]) * BM;
+        const int local = tile - p.meta[E + 1 + lo];
+        // 256-row CTAs: the CTA of an expert's even 128-row tile covers the odd one too
+        if (HALVES == 2 && (local & 1)) return;
+        m0 = p.meta[lo] + local * BM;
         m_end = p.meta[lo + 1];
         p.B += (size_t)lo * (p.K / Policy::kKPerWordRow) * p.N;
         p.S += (size_t)lo * (p.K / kGS) * p.N;
@@ -296,20 +299,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
         }
         if (tc::mbar_wait(acc_full, 0)) {
             tc::fence_after_sync();
+            // 32 x 32 blocks through a tile of this warp (the decode stages are free: every
+            // MMA is done), so that a warp's stores run along rows: lanes 0-15 and 16-31
+            // take column pairs of two rows
             const int quad = warp & 3, half = kc >> 2;
+            float *t = reinterpret_cast<float *>(smem + C::dec + kc * kEpiTileBytes);
 #pragma unroll 1
-            for (int c = 0; c < HALVES * BN / 2 / 16; ++c) {
-                const int h = c / (BN / 2 / 16);  // 128-row half of the tile
-                const int col = half * (BN / 2) + 16 * (c % (BN / 2 / 16));
-                const int m = m0 + h * BM + 32 * quad + lane;
-                float v[16];
-                tc::tmem_ld<16>(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(h * BN + col), v);
+            for (int c = 0; c < HALVES * BN / 2 / 32; ++c) {
+                const int h = c / (BN / 2 / 32);  // 128-row half of the tile
+                const int col = half * (BN / 2) + 32 * (c % (BN / 2 / 32));
+                float v[32];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(h * BN + col);
+                tc::tmem_ld<16>(taddr, *reinterpret_cast<float(*)[16]>(&v[0]));
+                tc::tmem_ld<16>(taddr + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
                 tc::tmem_wait_ld();
-                if (m < m_end && col < ncols) {
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2)
-                        epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, n0 + col + i, v[i], v[i + 1]);
-                }
+                epi_store_rows32<DT, POSTOP, OUT_F32>(t, v, p.C, p.Other, p.Bias, p.N, m0 + h * BM + 32 * quad, m_end,
+                                                      n0 + col, ncols - col, lane);
             }
         }
         pdl_launch_dependents();
@@ -330,6 +335,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
 // (many short tiles) and wherever the per-launch tile count leaves a ragged last wave.
 constexpr int kPEpiWarps = 4;
 constexpr int kPThreads = (2 + kDecWarps + kPEpiWarps) * 32;  // 448
+// Cfg<1>'s layout plus the epilogue warps' staging tiles (the next tile's mainloop owns
+// the decode stages while the epilogue runs)
+struct PSmem {
+    static constexpr int epi = Cfg<1>::bars + 256;
+    static constexpr int total = epi + kPEpiWarps * kEpiTileBytes + 1024;
+    static_assert(total <= 227 * 1024, "shared memory");
+};
 
 struct TileInfo {
     int m0, m_end, n0;
@@ -508,17 +520,16 @@ __global__ void __launch_bounds__(kPThreads, 1) gemm_persistent_kernel(const Par
             TileInfo ti;
             tile_info<Policy>(p, t, nN, ti);
             const int ncols = min(BN, p.N - ti.n0);
-            const int m = ti.m0 + 32 * quad + lane;
+            float *tt = reinterpret_cast<float *>(smem + PSmem::epi + quad * kEpiTileBytes);
 #pragma unroll 1
-            for (int c = 0; c < BN / 16; ++c) {
-                float v[16];
-                tc::tmem_ld<16>(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(b * BN + 16 * c), v);
+            for (int c = 0; c < BN / 32; ++c) {
+                float v[32];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(b * BN + 32 * c);
+                tc::tmem_ld<16>(taddr, *reinterpret_cast<float(*)[16]>(&v[0]));
+                tc::tmem_ld<16>(taddr + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
                 tc::tmem_wait_ld();
-                if (m < ti.m_end && 16 * c < ncols) {
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2)
-                        epi_store2<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, ti.n0 + 16 * c + i, v[i], v[i + 1]);
-                }
+                epi_store_rows32<DT, POSTOP, OUT_F32>(tt, v, p.C, p.Other, p.Bias, p.N, ti.m0 + 32 * quad, ti.m_end,
+                                                      ti.n0 + 32 * c, ncols - 32 * c, lane);
             }
             tc::fence_before_sync();
             __syncwarp();
@@ -566,9 +577,9 @@ cudaError_t launch_persistent(const GemvArgs &a, const int *meta = nullptr, int 
     return dispatch_epilogue<GemvArgs>(a, [&](auto dt, auto po, auto of) -> cudaError_t {
         using DT = typename decltype(dt)::type;
         auto kern = gemm_persistent_kernel<Policy, DT, decltype(po)::value, decltype(of)::value>;
-        cudaError_t err = ensure_smem(kern, Cfg<1>::total);
+        cudaError_t err = ensure_smem(kern, PSmem::total);
         if (err != cudaSuccess) return err;
-        return launch_kernel(kern, dim3(grid), dim3(kPThreads), (size_t)Cfg<1>::total, a.stream, p, map);
+        return launch_kernel(kern, dim3(grid), dim3(kPThreads), (size_t)PSmem::total, a.stream, p, map);
     });
 }
 
@@ -593,8 +604,9 @@ cudaError_t launch_policy(const GemvArgs &a, const int *meta = nullptr, int E = 
         auto kern = gemm_kernel<Policy, HALVES, DT, decltype(po)::value, decltype(of)::value>;
         cudaError_t err = ensure_smem(kern, Cfg<HALVES>::total);
         if (err != cudaSuccess) return err;
-        // grouped: every expert adds at most one partial row tile
-        const int rows = Cfg<HALVES>::kRows;
+        // grouped: one CTA per 128-row tile of meta (every expert adds at most one partial
+        // tile); dense: one per kRows rows
+        const int rows = meta ? BM : Cfg<HALVES>::kRows;
         const int tiles = (a.M + rows - 1) / rows + (meta ? E : 0);
         const dim3 grid((a.N + BN - 1) / BN, tiles);
         return launch_kernel(kern, grid, dim3(kThreads), (size_t)Cfg<HALVES>::total, a.stream, p, map);
@@ -606,7 +618,7 @@ cudaError_t launch_policy(const GemvArgs &a, const int *meta = nullptr, int E = 
 namespace gemm {
 // 128- or 256-row tiles: one CTA per SM, so a grid runs in ceil(tiles / SMs) waves; a
 // 256-row tile does twice the work of a 128-row one in ~1.6x the time (measured on
-// B200), so pick the shape with fewer wave-weighted units.  MoE tiles are 128 rows.
+// B200), so pick the shape with fewer wave-weighted units.
 bool use_256_rows(int M, int N) {
     if (options().gemm_tile_m) return options().gemm_tile_m == 256;
     if (M <= BM) return false;
@@ -632,9 +644,13 @@ cudaError_t int1_gemm_tc_launch(const GemvArgs &a) {
     return gemm::use_256_rows(a.M, a.N) ? gemm::launch_policy<gemm::Int1Gemm, 2>(a)
                                         : gemm::launch_policy<gemm::Int1Gemm, 1>(a);
 }
+// MoE: 256-row CTAs (two MMAs share each decoded B tile) once the experts average two
+// 128-row tiles, else 128-row ones (OPT_GEMM_TILE_M overrides)
 cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E) {
-    if (options().gemm_persistent == 0) return gemm::launch_policy<gemm::Int2Gemm, 1>(a, meta, E);
-    return gemm::launch_persistent<gemm::Int2Gemm>(a, meta, E);
+    if (options().gemm_persistent != 0) return gemm::launch_persistent<gemm::Int2Gemm>(a, meta, E);
+    const bool rows256 = options().gemm_tile_m ? options().gemm_tile_m == 256 : a.M >= 2 * gemm::BM * E;
+    return rows256 ? gemm::launch_policy<gemm::Int2Gemm, 2>(a, meta, E)
+                   : gemm::launch_policy<gemm::Int2Gemm, 1>(a, meta, E);
 }
 cudaError_t read_device_error_gemm_tc(unsigned *out, int reset) { return tc::read_tu_error(out, reset); }
 

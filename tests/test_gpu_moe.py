@@ -53,11 +53,14 @@ def expert_weights(rng, E, K, N, bf16):
     return B, S
 
 
-@pytest.fixture(params=[0, 1], ids=["one_cta_per_tile", "persistent"])
+@pytest.fixture(params=[(0, 128), (0, 256), (1, 0)], ids=["one_cta_per_tile", "rows256", "persistent"])
 def persistent(request, tl):
-    old = tl.set_option(tl.OPT_GEMM_PERSISTENT, request.param)
-    yield request.param
+    pers, tile = request.param
+    old = tl.set_option(tl.OPT_GEMM_PERSISTENT, pers)
+    old_tile = tl.set_option(tl.OPT_GEMM_TILE_M, tile)
+    yield pers
     tl.set_option(tl.OPT_GEMM_PERSISTENT, old)
+    tl.set_option(tl.OPT_GEMM_TILE_M, old_tile)
 
 
 @pytest.mark.parametrize("bf16", [0, 1])

@@ -41,7 +41,8 @@ struct BF16 {
 //   0 none, 1 v*sigmoid(v)*other, 2 v+other, 3 v+bias[n], 4 sigmoid(v);
 // sigmoid(x) = 0 for x <= -10 else 1/(exp(-x)+1)  (xetla_sigmoid).
 __device__ __forceinline__ float sigmoid_x(float x) {
-    return x <= -10.0f ? 0.0f : 1.0f / (expf(-x) + 1.0f);
+    // __frcp_rn(y) is the correctly rounded 1/y, the IEEE quotient 1.0f / y
+    return x <= -10.0f ? 0.0f : __frcp_rn(expf(-x) + 1.0f);
 }
 
 template <int POSTOP>
@@ -104,24 +105,65 @@ __device__ __forceinline__ void epi_store2(void *__restrict__ C, const uint16_t 
 // a TMEM lane holds them), stored along rows through the warp's shared tile t[32][33]
 // (conflict-free both ways): lanes 0-15 and 16-31 store column pairs of two rows at a
 // time, so a store instruction writes two contiguous row segments.  Rows from m_end on
-// and columns from ncols on (ncols even) are skipped.
+// and columns from ncols on (ncols even) are skipped.  For POSTOP 1/2 the block's 16 Other
+// pairs are loaded first (epi_load_rows32), all in flight together.
+template <int POSTOP>
+__device__ __forceinline__ void epi_load_rows32(uint32_t (&o)[16], const uint16_t *__restrict__ other, int N,
+                                                int mrow, int m_end, int n, int ncols, int lane) {
+    if constexpr (POSTOP == 1 || POSTOP == 2) {
+        const int rsub = lane >> 4, c2 = 2 * (lane & 15);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int r = 2 * i + rsub;
+            o[i] = (c2 < ncols && mrow + r < m_end)
+                       ? *reinterpret_cast<const uint32_t *>(other + (size_t)(mrow + r) * N + n + c2)
+                       : 0u;
+        }
+    }
+}
+
 template <class DT, int POSTOP, bool OUT_F32>
-__device__ __forceinline__ void epi_store_rows32(float *t, const float (&v)[32], void *__restrict__ C,
-                                                 const uint16_t *__restrict__ other, const void *__restrict__ bias,
-                                                 int N, int mrow, int m_end, int n, int ncols, int lane) {
+__device__ __forceinline__ void epi_store_rows32(float *t, const float (&v)[32], const uint32_t (&o)[16],
+                                                 void *__restrict__ C, const void *__restrict__ bias, int N, int mrow,
+                                                 int m_end, int n, int ncols, int lane) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) t[lane * 33 + j] = v[j];
     __syncwarp();
     const int rsub = lane >> 4, c2 = 2 * (lane & 15);
     if (c2 < ncols) {
-#pragma unroll 4
-        for (int rr = 0; rr < 32; rr += 2) {
-            const int r = rr + rsub;
-            if (mrow + r < m_end)
-                epi_store2<DT, POSTOP, OUT_F32>(C, other, bias, N, mrow + r, n + c2, t[r * 33 + c2], t[r * 33 + c2 + 1]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int r = 2 * i + rsub;
+            if (mrow + r < m_end) {
+                float v0 = t[r * 33 + c2], v1 = t[r * 33 + c2 + 1];
+                const size_t idx = (size_t)(mrow + r) * N + n + c2;
+                if constexpr (POSTOP == 1 || POSTOP == 2) {
+                    v0 = epi<POSTOP>(v0, DT::tof((uint16_t)(o[i] & 0xffffu)));
+                    v1 = epi<POSTOP>(v1, DT::tof((uint16_t)(o[i] >> 16)));
+                } else if constexpr (POSTOP == 3) {
+                    v0 = epi<POSTOP>(v0, epi_in<DT, POSTOP, OUT_F32>(nullptr, bias, idx, n + c2));
+                    v1 = epi<POSTOP>(v1, epi_in<DT, POSTOP, OUT_F32>(nullptr, bias, idx + 1, n + c2 + 1));
+                } else {
+                    v0 = epi<POSTOP>(v0, 0.0f);
+                    v1 = epi<POSTOP>(v1, 0.0f);
+                }
+                if constexpr (OUT_F32) *reinterpret_cast<float2 *>(reinterpret_cast<float *>(C) + idx) = make_float2(v0, v1);
+                else *reinterpret_cast<uint32_t *>(reinterpret_cast<uint16_t *>(C) + idx) =
+                    (uint32_t)DT::fromf(v0) | ((uint32_t)DT::fromf(v1) << 16);
+            }
         }
     }
     __syncwarp();
+}
+
+// both steps at once
+template <class DT, int POSTOP, bool OUT_F32>
+__device__ __forceinline__ void epi_store_rows32(float *t, const float (&v)[32], void *__restrict__ C,
+                                                 const uint16_t *__restrict__ other, const void *__restrict__ bias,
+                                                 int N, int mrow, int m_end, int n, int ncols, int lane) {
+    uint32_t o[16];
+    epi_load_rows32<POSTOP>(o, other, N, mrow, m_end, n, ncols, lane);
+    epi_store_rows32<DT, POSTOP, OUT_F32>(t, v, o, C, bias, N, mrow, m_end, n, ncols, lane);
 }
 constexpr int kEpiTileBytes = 32 * 33 * 4;
 

@@ -353,11 +353,15 @@ def run_moe(args, tl, synth, dev, world, rank, local):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
+        if args.profile_range:
+            torch.cuda.cudart().cudaProfilerStart()
         ev0.record(stream)
         for _ in range(args.steps):
             run()
         ev1.record(stream)
         barrier()
+        if args.profile_range:
+            torch.cuda.cudart().cudaProfilerStop()
     ms = ev0.elapsed_time(ev1) / args.steps
     # end to end: tokens in from pinned host memory, layer output back every step
     hX = X.cpu().pin_memory()
@@ -388,7 +392,8 @@ def run_moe(args, tl, synth, dev, world, rank, local):
                            "parallelism": "expert-parallel x%d, NCCL all-to-all" % world if world > 1 else "single GPU"},
                 "roofline": {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12 / world, "peak": pk[0],
                              "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / world / pk[0],
-                             "peak_kind": pk[1], "kernel": "gemm_kernel<Int2Gemm, 1> (grouped)", "traffic": None},
+                             "peak_kind": pk[1], "kernel": "gemm_kernel<Int2Gemm, HALVES> (grouped)",
+                             "traffic": None},
                 "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": hX.numel() * 2 * world,
                         "d2h_bytes_per_step": hO.numel() * 2 * world},
                 "gpu_launches": launches * args.steps, "clocks": clk.summary(),

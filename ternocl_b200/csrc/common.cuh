@@ -41,8 +41,9 @@ struct BF16 {
 //   0 none, 1 v*sigmoid(v)*other, 2 v+other, 3 v+bias[n], 4 sigmoid(v);
 // sigmoid(x) = 0 for x <= -10 else 1/(exp(-x)+1)  (xetla_sigmoid).
 __device__ __forceinline__ float sigmoid_x(float x) {
-    // __frcp_rn(y) is the correctly rounded 1/y, the IEEE quotient 1.0f / y
-    return x <= -10.0f ? 0.0f : __frcp_rn(expf(-x) + 1.0f);
+    // __expf (the hardware exp2 path, ~2 ulp) and the correctly rounded reciprocal: within
+    // a few fp32 ulp of the reference's 1/(exp(-x)+1), far inside the output tolerance
+    return x <= -10.0f ? 0.0f : __frcp_rn(__expf(-x) + 1.0f);
 }
 
 template <int POSTOP>

@@ -7,21 +7,21 @@
 // with the int8 activations Aq and scales SA of ternocl_int8_quant_a (host gold:
 // compute_gold, int2_via_int2_x_int8_dpas/main.cpp:94-121).
 //
-// CTA tile 128 (M) x 128 (N); one stage = one 128-row group (K = 128).  704 threads:
+// CTA tile 128 (M) x 128 (N); one stage = one 128-row group (K = 128).  576 threads:
 //   warp 0      producer: Aq [128 x 128] through a 2-D tensor map (one box of 128 rows x
 //               128 bytes in the 128-byte swizzle layout), the group's 8 packed word rows, the SB row
 //               and the tile's SA entries through 1-D bulk copies (5 stages);
 //   warp 1      TMEM (4 x 128 int32 columns) and the MMA issuer: per group four
 //               tcgen05.mma.cta_group::1.kind::i8 (M=128, N=128, K=32, s8 x s8 -> s32)
 //               into accumulator buffer g % 4;
-//   warps 2-5   decode (4 stages ahead of the MMA): thread n turns the 8 words of column n
-//               into 8 core-matrix rows of the K-major int8 B tile, 64 x the code value (code_to_value, main.cpp:77):
+//   warps 2-9   decode (4 stages ahead of the MMA): two threads per column n each turn 4
+//               of the column's 8 words into core-matrix rows of the K-major int8 B tile, 64 x the code value (code_to_value, main.cpp:77):
 //               one shift-and-mask per four rows leaves each code in the top two bits of
 //               a byte, then a 4x4 byte transpose puts the 16 rows of the word in order;
 //               and the group's SB row (fp32) and 1/SA of the tile's rows into a ring of
 //               its own, so that a load stage is free as soon as it is decoded;
-//   warps 6-21  promotion: after each group, tcgen05.ld of the int32 accumulator (warp w
-//               owns TMEM lanes 32(w%4).. and 32 of the columns), then
+//   warps 10-17 promotion: after each group, tcgen05.ld of the int32 accumulator (warp w
+//               owns TMEM lanes 32(w%4).. and 64 of the columns), then
 //               acc += float(dot) * (SB[g,n] * (1/SA[g,m])) in registers (the gold's
 //               formula; 1/SA is the IEEE quotient) on packed f32x2 arithmetic, and the
 //               buffer's columns are set back to the bit pattern of 1.5 * 2^23 for its
@@ -52,8 +52,10 @@ namespace gemm8 {
 
 constexpr int BM = 128, BN = 128, BK = 128;
 constexpr int kStages = 5, kDecStages = 4, kSclStages = 8;
-constexpr int kDecWarps = 4, kEpiWarps = 16;
-constexpr int kEpiCols = BN * 4 / kEpiWarps;  // accumulator columns per promotion warp (32)
+constexpr int kDecWarps = 8, kEpiWarps = 8;
+constexpr int kDecPerCol = kDecWarps * 32 / BN;         // decode threads per column (2)
+constexpr int kWordsPerThread = BK / 16 / kDecPerCol;   // word rows each decodes (4)
+constexpr int kEpiCols = BN * 4 / kEpiWarps;            // accumulator columns per promotion warp (64)
 constexpr int kThreads = (2 + kDecWarps + kEpiWarps) * 32;
 constexpr int kAStageBytes = BM * BK;  // int8 A: one 128-byte-swizzled box of 128 rows x 128 B
 constexpr int kDecLBO = 128, kDecSBO = BK / 16 * 128 + 16;            // 1040
@@ -61,7 +63,7 @@ constexpr int kDecStageBytes = (BN / 8) * kDecSBO;                     // 16640
 constexpr int kPackStageBytes = (BK / 16) * BN * 4;                    // 4096
 constexpr int kSbBytes = BN * 2, kSaBytes = (BM + 8) * 2 + 16;  // 16-byte multiple
 constexpr int kAccBufs = 4;  // accumulator buffers: the MMA runs up to 3 groups ahead of the promotion
-constexpr int kTmemCols = kAccBufs * BN;  // all 512 columns: one CTA per SM (704 threads x 80 registers)
+constexpr int kTmemCols = kAccBufs * BN;  // all 512 columns: one CTA per SM (576 threads, > 65536/2 registers)
 
 struct Smem {
     static constexpr int dec = 0;
@@ -77,7 +79,7 @@ struct Smem {
     static constexpr int total = bars + 256 + 1024;  // + alignment slack
 };
 
-static_assert(kStages * kAStageBytes >= kEpiWarps * 32 * 33 * 4, "epilogue tiles reuse the A stages");
+static_assert(kStages * kAStageBytes >= kEpiWarps * kEpiTileBytes, "epilogue tiles reuse the A stages");
 
 struct Params {
     const uint32_t *B;
@@ -270,8 +272,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
             }
         }
     } else if (warp < 2 + kDecWarps) {
-        // decode: thread n = column n of the tile, 8 word rows of the stage; and row n's scale
-        const int n = tid - 64;
+        // decode: thread (part, n) = word rows part * kWordsPerThread .. of column n of the
+        // tile; part 0 also converts SB[n], the last part row n's scale
+        const int n = (tid - 64) % BN, part = (tid - 64) / BN;
         for (int kb = 0; kb < nk; ++kb) {
             const int s = kb % kStages, d = kb % kDecStages, r = kb % kSclStages;
             if (!tc::mbar_wait(&full[s], (kb / kStages) & 1)) break;
@@ -280,15 +283,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
             const uint32_t *pk = reinterpret_cast<const uint32_t *>(smem + Smem::pack + s * kPackStageBytes);
             char *dst = smem + Smem::dec + d * kDecStageBytes + (n >> 3) * kDecSBO + (n & 7) * 16;
 #pragma unroll
-            for (int kc = 0; kc < BK / 16; ++kc) *reinterpret_cast<uint4 *>(dst + kc * 128) = s8x64_row(pk[kc * BN + n]);
+            for (int i = 0; i < kWordsPerThread; ++i) {
+                const int kc = part * kWordsPerThread + i;
+                *reinterpret_cast<uint4 *>(dst + kc * 128) = s8x64_row(pk[kc * BN + n]);
+            }
             // the SB row as fp32 (columns past the matrix hold stale values; never stored) and
             // row n's 1/SA (the IEEE quotient, as the gold) / 64 (exact: 64 * dot comes back)
             float *scl = reinterpret_cast<float *>(smem + Smem::scl + r * Smem::kSclBytes);
-            scl[n] = DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sb + s * kSbBytes)[n]);
-            const float sa = sa_off + n < nsa
-                                 ? DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sa + s * kSaBytes)[sa_off + n])
-                                 : 0.0f;
-            scl[BN + n] = (sa == 0.0f ? 0.0f : __frcp_rn(sa)) * 0.015625f;
+            if (part == 0) scl[n] = DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sb + s * kSbBytes)[n]);
+            if (part == kDecPerCol - 1) {
+                const float sa = sa_off + n < nsa
+                                     ? DT::tof(reinterpret_cast<const uint16_t *>(smem + Smem::sa + s * kSaBytes)[sa_off + n])
+                                     : 0.0f;
+                scl[BN + n] = (sa == 0.0f ? 0.0f : __frcp_rn(sa)) * 0.015625f;
+            }
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -356,17 +364,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_kernel(const Params p, co
             }
         }
         if (ok) {
-            // through a 32 x 32 tile of this warp (the load stages are free: every MMA is
-            // done), so that the stores run along the rows: lane j = column col0 + j
-            float *t = reinterpret_cast<float *>(smem + Smem::a) + ew * (32 * 33);
+            // 32 x 32 blocks through a tile of this warp (the load stages are free: every
+            // MMA is done), stored along rows
+            float *t = reinterpret_cast<float *>(smem + Smem::a + ew * kEpiTileBytes);
 #pragma unroll
-            for (int c = 0; c < kEpiCols; c += 2) f2_split(acc[c / 2], t[lane * 33 + c], t[lane * 33 + c + 1]);
-            __syncwarp();
-            const int n = n0 + col0 + lane;
-            const int rows = min(32, m_end - (m0 + 32 * quad));
-            if (col0 + lane < ncols)
-                for (int rr = 0; rr < rows; ++rr)
-                    epi_store<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m0 + 32 * quad + rr, n, t[rr * 33 + lane]);
+            for (int hc = 0; hc < kEpiCols; hc += 32) {
+                float v[32];
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) f2_split(acc[(hc + c) / 2], v[c], v[c + 1]);
+                epi_store_rows32<DT, POSTOP, OUT_F32>(t, v, p.C, p.Other, p.Bias, p.N, m0 + 32 * quad, m_end,
+                                                      n0 + col0 + hc, ncols - col0 - hc, lane);
+            }
         }
         pdl_launch_dependents();
     }

@@ -41,9 +41,10 @@ struct BF16 {
 //   0 none, 1 v*sigmoid(v)*other, 2 v+other, 3 v+bias[n], 4 sigmoid(v);
 // sigmoid(x) = 0 for x <= -10 else 1/(exp(-x)+1)  (xetla_sigmoid).
 __device__ __forceinline__ float sigmoid_x(float x) {
-    // __expf (the hardware exp2 path, ~2 ulp) and the correctly rounded reciprocal: within
-    // a few fp32 ulp of the reference's 1/(exp(-x)+1), far inside the output tolerance
-    return x <= -10.0f ? 0.0f : __frcp_rn(__expf(-x) + 1.0f);
+    // __expf (the hardware exp2 path, ~2 ulp) and __fdividef (the hardware reciprocal,
+    // ~2 ulp; the denominator stays in [1, e^10 + 1]): within a few fp32 ulp of the
+    // reference's 1/(exp(-x)+1), far inside the output tolerance
+    return x <= -10.0f ? 0.0f : __fdividef(1.0f, __expf(-x) + 1.0f);
 }
 
 template <int POSTOP>
@@ -155,6 +156,13 @@ __device__ __forceinline__ void epi_store_rows32(float *t, const float (&v)[32],
         }
     }
     __syncwarp();
+}
+
+// The 16 Other pairs of a 32 x 32 block from a shared copy os[32 rows][32 columns] (DT)
+__device__ __forceinline__ void epi_load_rows32_smem(uint32_t (&o)[16], const uint16_t *os, int lane) {
+    const int rsub = lane >> 4, c2 = 2 * (lane & 15);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = *reinterpret_cast<const uint32_t *>(os + (2 * i + rsub) * 32 + c2);
 }
 
 // both steps at once

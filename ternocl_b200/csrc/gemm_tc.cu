@@ -74,6 +74,8 @@ struct Cfg {
     static constexpr int bars = scale + kLoadStages * kScaleStageBytes;
     static constexpr int total = bars + 256 + 1024;  // + alignment slack
     static_assert(total <= 227 * 1024, "shared memory");
+    // the epilogue's Other ring (8 warps x 4 blocks of 32 x 32 DT) reuses the A stages
+    static_assert(kLoadStages * kAStageBytes >= 8 * 4 * 32 * 32 * 2, "Other ring");
 };
 
 struct Params {
@@ -304,18 +306,53 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const Params pin, con
             // take column pairs of two rows
             const int quad = warp & 3, half = kc >> 2;
             float *t = reinterpret_cast<float *>(smem + C::dec + kc * kEpiTileBytes);
+            constexpr int kChunks = HALVES * BN / 2 / 32;
+            auto chunk_row = [&](int c) { return m0 + (c / (BN / 2 / 32)) * BM + 32 * quad; };  // 128-row half
+            auto chunk_col = [&](int c) { return half * (BN / 2) + 32 * (c % (BN / 2 / 32)); };
+            // POSTOP 1/2: the Other blocks of the next kOtherRing chunks stream into a ring of
+            // this warp in the freed A stages (lane = row, 16-byte copies), so their latency
+            // overlaps the previous chunks' work (needs a 16-byte-aligned Other)
+            constexpr bool kOther = POSTOP == 1 || POSTOP == 2;
+            constexpr int kOtherRing = 4, kOtherBlock = 32 * 32;  // elements
+            const bool ring_ok = kOther && (reinterpret_cast<uintptr_t>(p.Other) & 15u) == 0;
+            uint16_t *oring = reinterpret_cast<uint16_t *>(smem + C::a) + kc * kOtherRing * kOtherBlock;
+            auto fetch = [&](int c) {
+                if (ring_ok && c < kChunks) {
+                    const int r = chunk_row(c) + lane, col = chunk_col(c);
+                    uint16_t *dst = oring + (c % kOtherRing) * kOtherBlock + lane * 32;
+                    if (r < m_end)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            if (col + 8 * q < ncols)
+                                tc::cp_async16(dst + 8 * q, p.Other + (size_t)r * p.N + n0 + col + 8 * q);
+                }
+                tc::cp_async_commit();
+            };
+            if (ring_ok)
+                for (int c = 0; c < kOtherRing; ++c) fetch(c);
 #pragma unroll 1
-            for (int c = 0; c < HALVES * BN / 2 / 32; ++c) {
-                const int h = c / (BN / 2 / 32);  // 128-row half of the tile
-                const int col = half * (BN / 2) + 32 * (c % (BN / 2 / 32));
+            for (int c = 0; c < kChunks; ++c) {
+                const int h = c / (BN / 2 / 32);
+                const int col = chunk_col(c);
                 float v[32];
                 const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(h * BN + col);
                 tc::tmem_ld<16>(taddr, *reinterpret_cast<float(*)[16]>(&v[0]));
                 tc::tmem_ld<16>(taddr + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
                 tc::tmem_wait_ld();
-                epi_store_rows32<DT, POSTOP, OUT_F32>(t, v, p.C, p.Other, p.Bias, p.N, m0 + h * BM + 32 * quad, m_end,
-                                                      n0 + col, ncols - col, lane);
+                if (ring_ok) {
+                    uint32_t o[16];
+                    tc::cp_async_wait<kOtherRing - 1>();  // chunk c's block has landed
+                    __syncwarp();
+                    epi_load_rows32_smem(o, oring + (c % kOtherRing) * kOtherBlock, lane);
+                    epi_store_rows32<DT, POSTOP, OUT_F32>(t, v, o, p.C, p.Bias, p.N, chunk_row(c), m_end, n0 + col,
+                                                          ncols - col, lane);
+                    fetch(c + kOtherRing);  // after the warp's reads of that slot (synced above)
+                } else {
+                    epi_store_rows32<DT, POSTOP, OUT_F32>(t, v, p.C, p.Other, p.Bias, p.N, chunk_row(c), m_end,
+                                                          n0 + col, ncols - col, lane);
+                }
             }
+            if (ring_ok) tc::cp_async_wait<0>();
         }
         pdl_launch_dependents();
     }

@@ -79,6 +79,16 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// 16-byte cp.async global -> shared (L2 only), its commit and bounded-depth wait
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 // ---- tensor memory -----------------------------------------------------------------
 // Allocation is warp-wide (one warp); the base address is written to *slot (smem).
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {

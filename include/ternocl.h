@@ -87,10 +87,11 @@ int ternocl_device_error(int reset);
  *  TERNOCL_OPT_GEMV_WARPS (default 0 = planned per shape): warps per CTA of the int2
  *    decode GEMV (4, 8 or 16), which split the CTA's K range (the reference's SGM/LS
  *    tile options have the same role).
- *  TERNOCL_OPT_GEMM_PERSISTENT (default 0): the persistent tcgen05 GEMM (one CTA per
+ *  TERNOCL_OPT_GEMM_PERSISTENT (default 3): the persistent tcgen05 GEMM (one CTA per
  *    SM over all tiles, epilogue overlapped with the next tile) for 0 = no GEMM,
- *    1 = the MoE grouped GEMMs, 2 = every prefill GEMM (measured slower than one CTA
- *    per tile on B200 for the shapes benchmarked here).
+ *    1 = the MoE grouped GEMMs, 2 = every prefill GEMM, 3 = the MoE grouped GEMMs with
+ *    K <= 1024 (a short main loop per tile: the MoE down projection; one CTA per tile
+ *    measured faster for the longer ones).
  *  TERNOCL_OPT_GEMV_IMPL (default 0 = chosen per M): the int2 decode GEMV used by
  *    ternocl_int2_upcvt at small M: 1 = fp16/bf16 MMA on decoded weights, 2 = integer
  *    MMA on int8 weights and exact fixed-point activations (M <= 4, the default there),

@@ -274,7 +274,7 @@ int ternocl_set_option(int option, int value) {
         return old;
     }
     if (option == TERNOCL_OPT_GEMM_PERSISTENT) {
-        if (value < 0 || value > 2) return -1;
+        if (value < 0 || value > 3) return -1;
         const int old = options().gemm_persistent;
         options().gemm_persistent = value;
         return old;

@@ -684,7 +684,9 @@ cudaError_t int1_gemm_tc_launch(const GemvArgs &a) {
 // MoE: 256-row CTAs (two MMAs share each decoded B tile) once the experts average two
 // 128-row tiles, else 128-row ones (OPT_GEMM_TILE_M overrides)
 cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E) {
-    if (options().gemm_persistent != 0) return gemm::launch_persistent<gemm::Int2Gemm>(a, meta, E);
+    const int pers = options().gemm_persistent;
+    if (pers == 1 || pers == 2 || (pers == 3 && a.K <= 1024))
+        return gemm::launch_persistent<gemm::Int2Gemm>(a, meta, E);
     const bool rows256 = options().gemm_tile_m ? options().gemm_tile_m == 256 : a.M >= 2 * gemm::BM * E;
     return rows256 ? gemm::launch_policy<gemm::Int2Gemm, 2>(a, meta, E)
                    : gemm::launch_policy<gemm::Int2Gemm, 1>(a, meta, E);

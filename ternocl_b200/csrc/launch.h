@@ -19,7 +19,8 @@ struct Options {
     int gemm_tile_m = 0;  // prefill GEMM CTA rows: 0 = per shape, 128 or 256
     int gemv_split = 0;   // decode GEMV K split: 0 = planned per shape
     int gemv_warps = 0;   // decode GEMV warps per CTA: 0 = planned per shape
-    int gemm_persistent = 0;  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every prefill GEMM
+    int gemm_persistent = 3;  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every prefill GEMM,
+                              // 3 MoE grouped GEMMs with K <= 1024
     int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA (M <= 4), 3 persistent (M = 1)
 };
 Options &options();

@@ -53,7 +53,7 @@ def expert_weights(rng, E, K, N, bf16):
     return B, S
 
 
-@pytest.fixture(params=[(0, 128), (0, 256), (1, 0)], ids=["one_cta_per_tile", "rows256", "persistent"])
+@pytest.fixture(params=[(0, 128), (0, 256), (1, 0), (3, 0)], ids=["one_cta_per_tile", "rows256", "persistent", "auto"])
 def persistent(request, tl):
     pers, tile = request.param
     old = tl.set_option(tl.OPT_GEMM_PERSISTENT, pers)

@@ -113,6 +113,29 @@ static GemvPlan gemv_plan(int M, int N, int K, bool allow_ws) {
     return p;
 }
 
+// integer-MMA GEMV (gemv_i2d.cu, M <= 4): measured on B200 over the Llama-3-8B decode
+// shapes with the launches replayed from a CUDA graph, a K split pays only when the
+// column strips fill less than half of the SMs (the cluster reduction costs more than
+// the extra CTAs give), and 8 warps per CTA beat 16 on K = 4096 (4 once the grid holds
+// >= 4 CTAs per SM): 4096x4096 6.7 -> 4.6 us, 4096x6144 6.6 -> 5.8 us, 14336x4096 9.6
+// -> 9.4 us.
+static GemvPlan gemv_digit_plan(int M, int N, int K, bool allow_ws) {
+    const int G = K / kGS, sms = sm_count();
+    const long long tiles = (long long)((N + 31) / 32) * ((M + 3) / 4);
+    int sk = options().gemv_split ? options().gemv_split : (2 * tiles < sms ? 2 : 1);
+    if (sk > G) sk = G;
+    const int warps = options().gemv_warps ? options().gemv_warps : (tiles >= 4LL * sms ? 4 : 8);
+    GemvPlan p;
+    p.SK = sk;
+    while (p.SK < G && int2_gemv_d_smem(M, K, p.SK, warps) > kGemvSmemBudget) ++p.SK;
+    if (p.SK > kMaxClusterSK && !allow_ws) p.SK = kMaxClusterSK;
+    p.cluster = p.SK > 1 && p.SK <= kMaxClusterSK;
+    p.cnt_bytes = round_up((size_t)tiles * sizeof(unsigned), 256);
+    p.part_bytes = (size_t)p.SK * M * N * sizeof(float);
+    p.warps = warps;
+    return p;
+}
+
 // int1 GEMV (gemv_int1.cu): same CTA shape
 static GemvPlan gemv_i1_plan(int M, int N, int K, bool allow_ws) {
     return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
@@ -195,8 +218,9 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
         return cuda_status(int2_gemv_p_launch(a));
     }
     const bool digit = M <= kGemvDigitMaxM && impl != 1;
-    GemvPlan p = gemv_plan(M, N, K, ws != nullptr);
-    if (p.total() > ws_bytes) p = gemv_plan(M, N, K, false);
+    auto plan = [&](bool allow_ws) { return digit ? gemv_digit_plan(M, N, K, allow_ws) : gemv_plan(M, N, K, allow_ws); };
+    GemvPlan p = plan(ws != nullptr);
+    if (p.total() > ws_bytes) p = plan(false);
     const size_t smem = digit ? int2_gemv_d_smem(M, K, p.SK, p.warps) : int2_gemv_smem(M, K, p.SK, p.warps);
     if (smem > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
     a.SK = p.SK;
@@ -310,6 +334,7 @@ size_t ternocl_gemv_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0 || N % 16 || K % kGS) return 0;
     // the largest need of the GEMVs that take a workspace (int2 on either path, int1)
     size_t need = gemv_plan(M, N, K, true).total();
+    if (M <= kGemvDigitMaxM && gemv_digit_plan(M, N, K, true).total() > need) need = gemv_digit_plan(M, N, K, true).total();
     const size_t b = gemv_tc_plan(M, N, K, true).total(), c = gemv_i1_plan(M, N, K, true).total();
     if (b > need) need = b;
     if (c > need) need = c;

@@ -91,16 +91,21 @@ static GemvPlan gemv_plan_t(int M, int N, int K, int cols, int rows, int per_sm,
 // PDL (M=1): splitting K across CTAs pays only while there are fewer column strips than
 // SMs (the cross-CTA reduction costs more than the parallelism otherwise); inside a CTA
 // 16 warps split K while the CTA streams <= 32 groups, 8 beyond that, and 4 once the
-// grid already holds >= 4 CTAs per SM (occupancy then matters more).
+// grid already holds >= 4 CTAs per SM (occupancy then matters more).  For M > 4 (this
+// kernel's default range since the integer-MMA GEMV took M <= 4), re-measured from CUDA
+// graph replays at M = 8: a two-way K split and 8 warps (4 at >= 4 CTAs per SM) --
+// 4096x6144 26.8 -> 8.9 us, 4096x4096 18.3 -> 6.9, 4096x28672 39.3 -> 34.1,
+// 14336x4096 19.7 -> 19.6 (16 warps were the slow part).
 static GemvPlan gemv_plan(int M, int N, int K, bool allow_ws) {
     const int G = K / kGS, sms = sm_count();
     const long long tiles = (long long)((N + 31) / 32) * ((M + 7) / 8);
-    int sk = options().gemv_split ? options().gemv_split : (tiles < sms ? 2 : 1);
+    const bool wide = M > kGemvDigitMaxM;
+    int sk = options().gemv_split ? options().gemv_split : (wide ? 2 : (tiles < sms ? 2 : 1));
     if (sk > G) sk = G;
     int warps = options().gemv_warps;
     if (!warps) {
         const int per_cta = (G + sk - 1) / sk;
-        warps = tiles >= 4LL * sms ? 4 : per_cta <= 32 ? 16 : 8;
+        warps = tiles >= 4LL * sms ? 4 : (wide || per_cta > 32) ? 8 : 16;
     }
     GemvPlan p;
     p.SK = sk;

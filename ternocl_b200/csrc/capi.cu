@@ -141,17 +141,34 @@ static GemvPlan gemv_digit_plan(int M, int N, int K, bool allow_ws) {
     return p;
 }
 
+// int1 and BITCOS GEMVs: measured from CUDA graph replays on the Llama-3-8B shapes and
+// the BITCOS 5376 x 21504 shape, a target of 3 CTAs per SM (the split of 6 per SM
+// over-split the narrow matrices: int1 M=1 4096x4096 6.5 -> 5.6 us, BITCOS 13.8 -> 11.2
+// us; int1 keeps 6 for M > 4) and at least a two-way K split (int1 at M > 4: M=8
+// 4096x28672 39.5 -> 28.3 us; BITCOS at every M: 5376x21504 stays on two splits).
+static int gemv_target_per_sm(int M) { return M <= kGemvDigitMaxM ? 3 : 6; }
+static void gemv_min_split(GemvPlan &p, int K) {
+    if (options().gemv_split || p.SK >= 2 || K / kGS < 2) return;
+    const size_t per_split = p.part_bytes / (p.SK > 0 ? p.SK : 1);
+    p.SK = 2;
+    p.cluster = true;  // 2 <= the cluster limit: reduced through distributed shared memory
+    p.part_bytes = 2 * per_split;
+}
+
 // int1 GEMV (gemv_int1.cu): same CTA shape
 static GemvPlan gemv_i1_plan(int M, int N, int K, bool allow_ws) {
-    return gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
-                       [&](int sk) { return int1_gemv_smem(M, K, sk); });
+    GemvPlan p = gemv_plan_t(M, N, K, 32, 8, gemv_target_per_sm(M), kMaxClusterSK, allow_ws, kGemvSmemBudget,
+                             [&](int sk) { return int1_gemv_smem(M, K, sk); });
+    if (M > kGemvDigitMaxM) gemv_min_split(p, K);
+    return p;
 }
 
 // BITCOS GEMV (gemv_bitcos.cu): same CTA shape, whole K range staged per CTA
 // (with the fused transform, K splits on HB boundaries: SK <= K / HB)
 static GemvPlan gemv_bitcos_plan(int M, int N, int K, bool allow_ws, int had_hb = 0) {
-    GemvPlan p = gemv_plan_t(M, N, K, 32, 8, 6, kMaxClusterSK, allow_ws, kGemvSmemBudget,
+    GemvPlan p = gemv_plan_t(M, N, K, 32, 8, 3, kMaxClusterSK, allow_ws, kGemvSmemBudget,
                              [&](int sk) { return bitcos_gemv_smem(M, K, sk, had_hb); });
+    gemv_min_split(p, K);
     if (had_hb && p.SK > K / had_hb) {
         p.SK = K / had_hb;
         p.cluster = p.SK > 1 && p.SK <= kMaxClusterSK;

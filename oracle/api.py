@@ -61,6 +61,7 @@ def orc():
             "orc_epilogue": (None, [i, i, vp, vp, vp, vp, i, i, i]),
             "orc_hadamard": (i, [vp, vp, vp, i, i, i, i, i]),
             "orc_moe_route": (None, [vp, i, i, i, vp, vp, vp]),
+            "orc_moe_dequant": (None, [vp, vp, i, i, i, vp, i]),
             "orc_moe_token_ref": (None, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp, i]),
             "orc_moe_decode_token_ref": (None, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp, i]),
         }
@@ -103,6 +104,8 @@ def ref():
             "ref_bitcos_decode_col": (None, [vp, sz, i, i, i, vp]),
             "ref_bitcos_gold": (None, [vp, vp, sz, vp, vp, i, i, i]),
             "ref_hadamard_fwht": (i, [vp, vp, vp, i, i, i, i, i]),
+            "ref_moe_dequant": (None, [vp, vp, i, i, i, vp]),
+            "ref_moe_fill": (None, [i, i, i, C.c_uint, vp, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
@@ -238,6 +241,14 @@ def moe_route(ids, E, rows_per_tile):
     return meta, perm, inv
 
 
+def moe_dequant(B, S, E, K, N, bf16):
+    """int2_moe/prefill.cpp:56-66: every weight of an expert projection, W [E, K, N] float32."""
+    B, S = _c(B, np.uint32), _c(S, np.uint16)
+    W = np.empty((E, K, N), np.float32)
+    orc().orc_moe_dequant(_p(B), _p(S), E, K, N, _p(W), int(bf16))
+    return W
+
+
 def moe_token_ref(X, ids, RW, Bg, Sg, Bu, Su, Bd, Sd, t, topk, H, I, bf16):
     args = [_c(X, np.uint16), _c(ids, np.int32), _c(RW, np.uint16), _c(Bg, np.uint32),
             _c(Sg, np.uint16), _c(Bu, np.uint32), _c(Su, np.uint16), _c(Bd, np.uint32),
@@ -337,6 +348,25 @@ class Ref:
         Cc = np.empty((M, N), np.float32)
         r.ref_bitcos_gold(_p(A), _p(buf), buf.size, _p(S), _p(Cc), M, K, N)
         return Cc
+
+    @staticmethod
+    def moe_dequant(B, S, E, K, N, bf16):
+        r = ref()
+        r.ref_set_bf16(int(bf16))
+        B, S = _c(B, np.uint32), _c(S, np.uint16)
+        W = np.empty((E, K, N), np.float32)
+        r.ref_moe_dequant(_p(B), _p(S), E, K, N, _p(W))
+        return W
+
+    @staticmethod
+    def moe_fill(E, K, N, seed, bf16):
+        """The driver's generator (std::mt19937(seed), fill_proj): B [E, K/16, N], S [E, K/128, N]."""
+        r = ref()
+        r.ref_set_bf16(int(bf16))
+        B = np.empty((E, K // 16, N), np.uint32)
+        S = np.empty((E, K // 128, N), np.uint16)
+        r.ref_moe_fill(E, K, N, int(seed), _p(B), _p(S))
+        return B, S
 
     @staticmethod
     def epilogue(postop, out_f32, acc, other, bias, M, N, bf16):

@@ -359,6 +359,13 @@ static float proj_w(const uint32_t *B, const uint16_t *S, int K, int N, int e, i
            orc_tof(S[((size_t)e * (K / GS) + k / GS) * N + n], bf16);
 }
 
+/* W[e][k][n] = proj_w(e, k, n) over a whole [E, K/16, N] projection (the pin of proj_w) */
+void orc_moe_dequant(const uint32_t *B, const uint16_t *S, int E, int K, int N, float *W, int bf16) {
+    for (int e = 0; e < E; ++e)
+        for (int k = 0; k < K; ++k)
+            for (int n = 0; n < N; ++n) W[((size_t)e * K + k) * N + n] = proj_w(B, S, K, N, e, k, n, bf16);
+}
+
 /* int2_moe/prefill.cpp:291-310: o[n] = sum_j RW[g] * down(h),
  * h = DT(silu(gate.x) * DT(up.x)) in double precision */
 void orc_moe_token_ref(const uint16_t *X, const int *ids, const uint16_t *RW, const uint32_t *Bg,

@@ -62,6 +62,8 @@ int orc_hadamard(const uint16_t *x, const int8_t *signs, uint16_t *y, int rows, 
 
 /* MoE prefill routing with a stable (ascending g) order inside each expert. */
 void orc_moe_route(const int *ids, int G, int E, int rows_per_tile, int *meta, int *perm, int *inv);
+/* Every weight of a [E, K/16, N] int2 projection with [E, K/128, N] scales, as floats. */
+void orc_moe_dequant(const uint32_t *B, const uint16_t *S, int E, int K, int N, float *W, int bf16);
 /* The reference driver's double-precision check of token t's layer output o[H]. */
 void orc_moe_token_ref(const uint16_t *X, const int *ids, const uint16_t *RW, const uint32_t *Bg,
                        const uint16_t *Sg, const uint32_t *Bu, const uint16_t *Su,

@@ -3,12 +3,13 @@
 
 The outputs come from oracle/_ref/libternocl_ref.so, i.e. the reference drivers'
 host gold (compute_gold / epilogue_ref / compute_scale_a / to_sel_layout), its BITCOS
-packer and decoder (common/bitcos.hpp) and its Hadamard kernel source run on the CPU
-(hadamard/hadamard_fwht.cl).  It needs oracle/_ref built from the reference tree
+packer and decoder (common/bitcos.hpp), its Hadamard kernel source run on the CPU
+(hadamard/hadamard_fwht.cl) and the MoE driver's expert-weight decode and generator
+(int2_moe/prefill.cpp Proj::w, fill_proj).  It needs oracle/_ref built from the reference tree
 (`make -C oracle`), so it runs where the reference sources exist; the .npz fixtures
 it writes are committed and pin the oracle everywhere else.
 
-  python tests/golden/make_golden.py
+  python tests/golden/make_golden.py [int2 int1 int8 bitcos hadamard moe]
 """
 import ctypes
 import os
@@ -119,12 +120,35 @@ def hadamard_cases(R):
     return out
 
 
+def moe_cases(R):
+    # int2_moe/prefill.cpp:56-79: the expert projections' layout ([E, K/16, N] words,
+    # [E, K/128, N] scales) through the driver's own Proj::w, on its own generator's output
+    # (fill_proj, codes {0, 1, 3}) and on random words (code 2 as well)
+    out = {}
+    E, K, N = 3, 256, 16
+    for bf16 in (0, 1):
+        key = "moe_%s" % ("bf16" if bf16 else "fp16")
+        B, S = R.moe_fill(E, K, N, 42, bf16)
+        rng = np.random.default_rng(6000 + bf16)
+        Br = rng.integers(0, 2 ** 32, size=B.shape, dtype=np.uint64).astype(np.uint32)
+        out[key + "_B"], out[key + "_S"], out[key + "_Br"] = B, S, Br
+        out[key + "_W"] = R.moe_dequant(B, S, E, K, N, bf16)
+        out[key + "_Wr"] = R.moe_dequant(Br, S, E, K, N, bf16)
+    return out
+
+
+CASES = [("int2", int2_cases), ("int1", int1_cases), ("int8", int8_cases), ("bitcos", bitcos_cases),
+         ("hadamard", hadamard_cases), ("moe", moe_cases)]
+
+
 def main():
+    """Writes every fixture, or only those named on the command line (e.g. `moe`)."""
     if not api.ref_available():
         sys.exit("oracle/_ref not built: run `make -C oracle` where the reference tree exists")
     R = api.Ref
-    for name, fn in [("int2", int2_cases), ("int1", int1_cases), ("int8", int8_cases),
-                     ("bitcos", bitcos_cases), ("hadamard", hadamard_cases)]:
+    for name, fn in CASES:
+        if len(sys.argv) > 1 and name not in sys.argv[1:]:
+            continue
         d = fn(R)
         path = os.path.join(HERE, "golden_%s.npz" % name)
         np.savez_compressed(path, **d)

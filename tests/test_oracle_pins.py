@@ -1,6 +1,7 @@
 """Pin the oracle (oracle/oracle.c, the C restatement) against the reference's own
 code: the committed golden fixtures (made by tests/golden/make_golden.py from
-oracle/_ref, i.e. the reference host gold, BITCOS packer and Hadamard kernel source)
+oracle/_ref, i.e. the reference host gold, BITCOS packer, Hadamard kernel source and
+MoE expert-weight decode)
 and, where oracle/_ref is built, fresh random cases.  Bit-exact throughout."""
 import ctypes
 import os
@@ -112,6 +113,33 @@ def test_random_cases_vs_reference_build(bf16):
     assert same_bits(orc.int8_gold(Af, B, SA, S, M, K, N, bf16), orc.Ref.int8_gold(Af, B, SA, S, M, K, N, bf16))
     buf = orc.Ref.bitcos_random(K, N, 0.4, 3)
     assert same_bits(orc.bitcos_gold(A, buf, S, M, K, N, bf16), orc.Ref.bitcos_gold(A, buf, S, M, K, N, bf16))
+
+
+def test_moe_expert_weight_decode():
+    # int2_moe/prefill.cpp:56-66 (Proj::w): the [E, K/16, N] / [E, K/128, N] expert layout
+    # that the MoE token reference and the grouped kernels read
+    d = load("moe")
+    for bf16 in (0, 1):
+        k = "moe_%s" % ("bf16" if bf16 else "fp16")
+        B, S, Br = d[k + "_B"], d[k + "_S"], d[k + "_Br"]
+        E, K, N = B.shape[0], B.shape[1] * 16, B.shape[2]
+        assert same_bits(orc.moe_dequant(B, S, E, K, N, bf16), d[k + "_W"]), k
+        assert same_bits(orc.moe_dequant(Br, S, E, K, N, bf16), d[k + "_Wr"]), k
+        # the fixture holds the driver's generator output: codes {0, 1, 3} only
+        codes = np.stack([(B >> (2 * j)) & 3 for j in range(16)])
+        assert set(np.unique(codes).tolist()) == {0, 1, 3}
+        # the per-expert reading of the test generator (synth) agrees with Proj::w
+        W = d[k + "_Wr"]
+        for e in range(E):
+            Se = np.repeat(synth.from_dt(S[e], bf16), 128, axis=0)
+            assert same_bits((synth.unpack_int2(Br[e], K, N) * Se).astype(np.float32), W[e]), (k, e)
+
+
+@pytest.mark.skipif(not orc.ref_available(), reason="oracle/_ref (reference build) not present")
+def test_moe_decode_vs_reference_build():
+    for bf16 in (0, 1):
+        B, S = orc.Ref.moe_fill(5, 384, 48, 7 + bf16, bf16)
+        assert same_bits(orc.moe_dequant(B, S, 5, 384, 48, bf16), orc.Ref.moe_dequant(B, S, 5, 384, 48, bf16))
 
 
 def test_int2_value_matches_code_to_value():

@@ -88,6 +88,32 @@ def test_grouped_gemm(cuda, tl, persistent, bf16, postop, out_f32):
 
 
 @pytest.mark.parametrize("bf16", [0, 1])
+def test_grouped_gemm_decode_bit_exact(cuda, tl, persistent, bf16):
+    # every routed expert gets the K x K identity as its rows, so its output block is its
+    # decoded weight matrix: C[r0 + k, n] = code(k, n) * S[k/128, n] through one non-zero
+    # term, exact in fp32.  Compared bit for bit with the expert-weight decode of
+    # int2_moe/prefill.cpp:56-66 (Proj::w); random words, so every 2-bit code; expert 3
+    # gets no rows
+    rng = np.random.default_rng(50 + bf16)
+    E, K, N = 6, 256, 144
+    used = [0, 1, 2, 4, 5]
+    ids = np.repeat(np.array(used, np.int32), K)
+    B = rng.integers(0, 1 << 32, size=(E, K // 16, N), dtype=np.uint64).astype(np.uint32)
+    S = np.stack([synth.scales(rng, K, N, bf16) for _ in range(E)])
+    A = np.tile(synth.to_dt(np.eye(K), bf16), (len(used), 1))
+    meta, _, _ = tl.moe_route(dev_any(ids), E)
+    C = host_dt(tl.moe_gemm(meta, dev_dt(A, bf16), dev_u32(B), dev_dt(S, bf16), E, out_f32=True))
+    W = orc.moe_dequant(B, S, E, K, N, bf16)
+    m = meta.cpu().numpy()
+    assert m[3] == m[4]
+    for e in used:
+        r0, r1 = int(m[e]), int(m[e + 1])
+        assert r1 - r0 == K
+        assert np.array_equal(C[r0:r1].view(np.uint32), W[e].view(np.uint32)), "expert %d" % e
+    assert tl.device_error() == 0
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
 def test_layer_vs_token_reference(cuda, tl, persistent, bf16):
     # prefill.cpp's layer: up = gemm(Xs, Bu), H = gemm(Xs, Bg, POSTOP 1, Other = up),
     # Y = gemm(H, Bd, OUT_F32), O = combine(Y)

@@ -21,6 +21,8 @@ from the 126 MB L2).  One step = one GEMV per shape, each on the next weight set
 Secondary figure on the same line (`secondary.prefill`, 1 GPU): the M=2048 int2 fp16
 prefill GEMM (tcgen05) on the same four shapes, TFLOP/s (2*M*N*K per GEMM) against the
 measured sustained bf16 GEMM peak.  `--workload prefill` makes it the headline instead.
+`--workload moe` times the MoE prefill layer, `--workload hadamard` the sign flip + FWHT of
+the BITCOS config (rows 1, 8 and 512; HBM GB/s).
 
 With N GPUs (torchrun) the weight columns of every layer are split across the ranks
 and the outputs are all-gathered over NCCL inside the timed region (strong scaling).
@@ -440,6 +442,97 @@ def run_prefill(args, tl, synth, dev, world, rank, local):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- Hadamard
+# The BITCOS config's pre-transform: K = 5376 with HB = 256, the largest power-of-two
+# block dividing K (the config's HB = 1024 does not divide 5376), fp16, sign flip on.
+HAD = dict(K=5376, HB=256, rows=(1, 8, 512))
+HAD_SET_BYTES = 256 << 20  # distinct input rows streamed per row count (2x the L2)
+
+
+def run_hadamard(args, tl, synth, dev, world, rank, local):
+    """--workload hadamard: ternocl_hadamard_fwht at rows 1, 8 and 512.  One step = one
+    call per row count, each on the next of enough distinct input sets to stream
+    HAD_SET_BYTES, so no set is read from L2 again.  Bytes per call (algorithmic):
+    rows*K*2 read + rows*K*2 written + K sign bytes.  One GPU: each row count's K timed
+    calls are one CUDA-graph replay (the first replay, which uploads the graph, untimed).
+    N GPUs: independent replicas (weak scaling), time = max over ranks."""
+    import torch
+    import torch.distributed as dist
+    K, HB = HAD["K"], HAD["HB"]
+    rng = np.random.default_rng(11)
+    signs = torch.from_numpy(np.where(rng.random(K) < 0.5, -1, 1).astype(np.int8)).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    per = []  # (rows, bytes per call, ms per call)
+    with ClockSampler(local) as clk:
+        for rows in HAD["rows"]:
+            nsets = max(1, -(-HAD_SET_BYTES // (rows * K * 2)))
+            X = torch.randn(nsets * rows, K, device=dev, dtype=torch.float16)
+            Y = torch.empty_like(X)
+
+            def call(i, cs=None):
+                s = (i % nsets) * rows
+                tl.hadamard_fwht(X[s:s + rows], HB, signs, out=Y[s:s + rows], stream=cs)
+
+            for i in range(args.warmup):
+                call(nsets - 1 - i % nsets)
+            torch.cuda.synchronize()
+            graph = None
+            if world == 1 and args.graph:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    cs = torch.cuda.current_stream(dev).cuda_stream
+                    for i in range(args.steps):
+                        call(i, cs)
+                graph.replay()  # upload
+                torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier(device_ids=[local])
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if args.profile_range:
+                torch.cuda.cudart().cudaProfilerStart()
+            ev0.record(stream)
+            if graph is not None:
+                graph.replay()
+            else:
+                for i in range(args.steps):
+                    call(i)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            if args.profile_range:
+                torch.cuda.cudart().cudaProfilerStop()
+            ms = ev0.elapsed_time(ev1) / args.steps
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            per.append((rows, 2 * rows * K * 2 + K, ms))
+            del graph, X, Y
+            torch.cuda.empty_cache()
+    step_bytes = sum(b for _, b, _ in per)
+    step_ms = sum(ms for _, _, ms in per)
+    peak, peak_kind = peaks()
+    rows_d, bytes_d, ms_d = max(per, key=lambda p: p[2])  # the dominant launch
+    if rank == 0:
+        line = {"metric": "Hadamard sign flip + FWHT HBM GB/s", "value": world * step_bytes / (step_ms * 1e-3) / 1e9,
+                "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+                "data": "synthetic",
+                "config": {"workload": "hadamard_fwht of the BITCOS config (configs[3]): K=5376, HB=256, signs",
+                           "rows": list(HAD["rows"]),
+                           "l2": "inputs larger than L2: %d MiB of distinct rows per row count" % (HAD_SET_BYTES >> 20),
+                           "parallelism": "replicas x%d" % world if world > 1 else "single GPU",
+                           "per_rows": [{"rows": r, "us_per_call": ms * 1e3, "GBps": b / (ms * 1e-3) / 1e9}
+                                        for r, b, ms in per]},
+                "roofline": {"bound": "hbm", "achieved": bytes_d / (ms_d * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": bytes_d / (ms_d * 1e-3) / 1e9 / peak, "peak_kind": peak_kind,
+                             "kernel": "hadamard_fwht (rows=%d)" % rows_d, "traffic": None},
+                "gpu_launches": args.steps * len(per), "clocks": clk.summary(), "cpu_baseline": None}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -451,9 +544,10 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "moe"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "moe", "hadamard"],
                     help="decode: the headline M=1 GEMV sweep (+ prefill and MoE as secondary figures); "
-                         "prefill: the M=2048 GEMMs alone; moe: the MoE prefill layer (expert-parallel on N GPUs)")
+                         "prefill: the M=2048 GEMMs alone; moe: the MoE prefill layer (expert-parallel on N GPUs); "
+                         "hadamard: the sign flip + FWHT of the BITCOS config")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="N>1: GEMV + NCCL all-gather instead of the GEMV with the all-gather fused in its epilogue")
@@ -488,6 +582,8 @@ def main():
         return run_prefill(args, tl, synth, dev, world, rank, local)
     if args.workload == "moe":
         return run_moe(args, tl, synth, dev, world, rank, local)
+    if args.workload == "hadamard":
+        return run_hadamard(args, tl, synth, dev, world, rank, local)
 
     # per-rank column slices (multiples of 16)
     def cols(N):

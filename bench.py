@@ -512,6 +512,12 @@ def run_hadamard(args, tl, synth, dev, world, rank, local):
     step_ms = sum(ms for _, _, ms in per)
     peak, peak_kind = peaks()
     rows_d, bytes_d, ms_d = max(per, key=lambda p: p[2])  # the dominant launch
+    traffic = None  # DRAM bytes per 512-row launch from the committed ncu summary
+    tp = os.path.join(ROOT, "profiles", "hadamard_traffic.json")
+    if rows_d == 512 and os.path.exists(tp):
+        with open(tp) as f:
+            tb = json.load(f)["dram_bytes_per_launch"]
+        traffic = sum(tb) / len(tb)
     if rank == 0:
         line = {"metric": "Hadamard sign flip + FWHT HBM GB/s", "value": world * step_bytes / (step_ms * 1e-3) / 1e9,
                 "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
@@ -525,7 +531,7 @@ def run_hadamard(args, tl, synth, dev, world, rank, local):
                                         for r, b, ms in per]},
                 "roofline": {"bound": "hbm", "achieved": bytes_d / (ms_d * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
                              "frac": bytes_d / (ms_d * 1e-3) / 1e9 / peak, "peak_kind": peak_kind,
-                             "kernel": "hadamard_fwht (rows=%d)" % rows_d, "traffic": None},
+                             "kernel": "hadamard_fwht (rows=%d)" % rows_d, "traffic": traffic},
                 "gpu_launches": args.steps * len(per), "clocks": clk.summary(), "cpu_baseline": None}
         print(json.dumps(line), flush=True)
     if world > 1:

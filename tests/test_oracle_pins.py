@@ -135,6 +135,39 @@ def test_moe_expert_weight_decode():
             assert same_bits((synth.unpack_int2(Br[e], K, N) * Se).astype(np.float32), W[e]), (k, e)
 
 
+@pytest.mark.parametrize("bf16", [0, 1])
+def test_moe_token_ref_matches_its_parts(bf16):
+    # the token check of int2_moe/prefill.cpp:291-310, recomputed in numpy on top of the
+    # pinned expert decode: h = DT(silu(x.Wg) * DT(x.Wu)) per routed expert, o = sum over
+    # the token's experts of RW[g] * (h . Wd), all sums in double
+    rng = np.random.default_rng(90 + bf16)
+    T, topk, E, H, I = 3, 2, 4, 256, 128
+    ids = np.stack([rng.permutation(E)[:topk] for _ in range(T)]).reshape(-1).astype(np.int32)
+    X = synth.activations(rng, T, H, bf16)
+
+    def proj(K, N):
+        B = rng.integers(0, 2 ** 32, size=(E, K // 16, N), dtype=np.uint64).astype(np.uint32)
+        return B, np.stack([synth.scales(rng, K, N, bf16) for _ in range(E)])
+
+    (Bg, Sg), (Bu, Su), (Bd, Sd) = proj(H, I), proj(H, I), proj(I, H)
+    RW = synth.to_dt(rng.uniform(0.05, 1.0, T * topk), bf16)
+    Wg = orc.moe_dequant(Bg, Sg, E, H, I, bf16).astype(np.float64)
+    Wu = orc.moe_dequant(Bu, Su, E, H, I, bf16).astype(np.float64)
+    Wd = orc.moe_dequant(Bd, Sd, E, I, H, bf16).astype(np.float64)
+    dt = lambda v: synth.from_dt(synth.to_dt(v, bf16), bf16).astype(np.float64)  # noqa: E731
+    for t in range(T):
+        x = synth.from_dt(X[t], bf16).astype(np.float64)
+        o = np.zeros(H)
+        for j in range(topk):
+            g = t * topk + j
+            e = ids[g]
+            sg, su = x @ Wg[e], x @ Wu[e]
+            h = dt(sg / (1.0 + np.exp(-sg)) * dt(su))
+            o += (h @ Wd[e]) * float(synth.from_dt(RW[g:g + 1], bf16)[0])
+        ref = orc.moe_token_ref(X, ids, RW, Bg, Sg, Bu, Su, Bd, Sd, t, topk, H, I, bf16)
+        np.testing.assert_allclose(ref, o, rtol=1e-9, atol=1e-12 * np.abs(o).max())
+
+
 @pytest.mark.skipif(not orc.ref_available(), reason="oracle/_ref (reference build) not present")
 def test_moe_decode_vs_reference_build():
     for bf16 in (0, 1):

@@ -1,8 +1,9 @@
 """Pin the oracle (oracle/oracle.c, the C restatement) against the reference's own
 code: the committed golden fixtures (made by tests/golden/make_golden.py from
 oracle/_ref, i.e. the reference host gold, BITCOS packer, Hadamard kernel source and
-MoE expert-weight decode)
-and, where oracle/_ref is built, fresh random cases.  Bit-exact throughout."""
+MoE expert-weight decode) and, where oracle/_ref is built, fresh random cases, bit for
+bit; the MoE token references, which the reference runs inline in its drivers, against
+a numpy recomputation over the pinned decode to 1e-9 (double sums in another order)."""
 import ctypes
 import os
 
@@ -135,11 +136,13 @@ def test_moe_expert_weight_decode():
             assert same_bits((synth.unpack_int2(Br[e], K, N) * Se).astype(np.float32), W[e]), (k, e)
 
 
+@pytest.mark.parametrize("decode", [False, True], ids=["prefill", "decode"])
 @pytest.mark.parametrize("bf16", [0, 1])
-def test_moe_token_ref_matches_its_parts(bf16):
-    # the token check of int2_moe/prefill.cpp:291-310, recomputed in numpy on top of the
-    # pinned expert decode: h = DT(silu(x.Wg) * DT(x.Wu)) per routed expert, o = sum over
-    # the token's experts of RW[g] * (h . Wd), all sums in double
+def test_moe_token_ref_matches_its_parts(bf16, decode):
+    # the token checks of int2_moe/prefill.cpp:291-310 and int2_moe/main.cpp:267-291,
+    # recomputed in numpy on top of the pinned expert decode: h = DT(silu(x.Wg) * DT(x.Wu))
+    # per routed expert (the decode driver does not round x.Wu to DT), o = sum over the
+    # token's experts of RW[g] * (h . Wd), all sums in double
     rng = np.random.default_rng(90 + bf16)
     T, topk, E, H, I = 3, 2, 4, 256, 128
     ids = np.stack([rng.permutation(E)[:topk] for _ in range(T)]).reshape(-1).astype(np.int32)
@@ -162,9 +165,10 @@ def test_moe_token_ref_matches_its_parts(bf16):
             g = t * topk + j
             e = ids[g]
             sg, su = x @ Wg[e], x @ Wu[e]
-            h = dt(sg / (1.0 + np.exp(-sg)) * dt(su))
+            h = dt(sg / (1.0 + np.exp(-sg)) * (su if decode else dt(su)))
             o += (h @ Wd[e]) * float(synth.from_dt(RW[g:g + 1], bf16)[0])
-        ref = orc.moe_token_ref(X, ids, RW, Bg, Sg, Bu, Su, Bd, Sd, t, topk, H, I, bf16)
+        fn = orc.moe_decode_token_ref if decode else orc.moe_token_ref
+        ref = fn(X, ids, RW, Bg, Sg, Bu, Su, Bd, Sd, t, topk, H, I, bf16)
         np.testing.assert_allclose(ref, o, rtol=1e-9, atol=1e-12 * np.abs(o).max())
 
 

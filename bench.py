@@ -62,14 +62,72 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def peaks_tensor():
-    """Dense bf16 GEMM peak: the sustained figure (the GEMMs run back to back for a whole step)."""
+def peaks_tensor(region_s):
+    """Dense bf16 GEMM peak for a timed region of `region_s` seconds: the burst figure
+    under a second (the clocks have not settled under the power cap yet), the sustained
+    figure for longer regions."""
+    burst = region_s < 1.0
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
+        if burst:
+            return d["bf16_tflops"], "measured burst"
         return d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured sustained"
-    return 1400.0, "fallback sustained"
+    return (1590.0, "fallback burst") if burst else (1400.0, "fallback sustained")
+
+
+def peaks_int8(region_s):
+    """Dense int8 tensor peak: twice the bf16 figure (the nominal dense rates are 4.5 POPS
+    int8 against 2.25 PFLOP/s bf16 on B200); no int8 GEMM is measured by the pool."""
+    v, kind = peaks_tensor(region_s)
+    return 2.0 * v, "2 x %s bf16 GEMM (int8:bf16 nominal dense ratio)" % kind
+
+
+def time_events(stream, fn, reps):
+    """ms per call of fn() (launches on `stream`), CUDA events around `reps` calls."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def device_int2_words(K, N, gen, dev):
+    """Uniform ternary int2 words [K/16, N] (codes {0, 1, 3}) generated on the device."""
+    import torch
+    out = torch.empty(K // 16, N, dtype=torch.int32, device=dev)
+    shifts = (2 * torch.arange(16, device=dev, dtype=torch.int64)).view(1, 16, 1)
+    rows = max(1, (1 << 24) // (16 * N))
+    for r0 in range(0, K // 16, rows):
+        r1 = min(K // 16, r0 + rows)
+        c = torch.randint(0, 3, (r1 - r0, 16, N), generator=gen, device=dev, dtype=torch.int64)
+        c = torch.where(c == 2, torch.full_like(c, 3), c)
+        w = (c << shifts).sum(dim=1)
+        out[r0:r1] = torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)
+    return out
+
+
+def check(tl, name, st):
+    if st != 0:
+        raise tl.TernoclError(name, st)
+
+
+def cpu_loop(fn, budget_s):
+    """Runs fn() (one bounded unit of CPU work) until budget_s has passed; returns
+    (units done, seconds)."""
+    fn()  # warm-up (page-in, thread pool)
+    n, el = 0, 0.0
+    while el < budget_s:
+        t0 = time.perf_counter()
+        fn()
+        el += time.perf_counter() - t0
+        n += 1
+    return n, el
 
 
 def profile_traffic():
@@ -303,8 +361,10 @@ def moe_layer(tl, m, stream=None):
     tl.moe_combine(m["Y"], inv, m["RW"], MOE["T"], topk, out=m["O"], stream=stream)
 
 
-def moe_measure(tl, synth, dev, steps, warmup):
-    """(tokens/s, TFLOP/s, ms per layer) of the C5 MoE prefill layer."""
+def moe_measure(tl, synth, dev, steps, warmup, cpu=True):
+    """(tokens/s, TFLOP/s, ms per layer, e2e dict, cpu_baseline dict) of the C5 MoE prefill
+    layer; e2e: the tokens copied in from pinned host memory and the layer output copied
+    back every step."""
     import torch
     m = moe_setup(tl, synth, dev)
     for _ in range(warmup):
@@ -320,7 +380,18 @@ def moe_measure(tl, synth, dev, steps, warmup):
     ms = ev0.elapsed_time(ev1) / steps
     G = MOE["T"] * MOE["topk"]
     flops = 2.0 * G * (2 * MOE["H"] * MOE["I"] + MOE["I"] * MOE["H"])
-    return MOE["T"] / (ms * 1e-3), flops / (ms * 1e-3) / 1e12, ms
+    hX = m["X"].cpu().pin_memory()
+    hO = torch.empty(m["O"].shape, dtype=m["O"].dtype).pin_memory()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        m["X"].copy_(hX, non_blocking=True)
+        moe_layer(tl, m)
+        hO.copy_(m["O"], non_blocking=True)
+        stream.synchronize()
+    e2e_s = (time.perf_counter() - t0) / steps
+    e2e = {"value": MOE["T"] / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": hX.numel() * 2,
+           "d2h_bytes_per_step": hO.numel() * 2}
+    return MOE["T"] / (ms * 1e-3), flops / (ms * 1e-3) / 1e12, ms, e2e, (moe_cpu_baseline(m) if cpu else None)
 
 
 def run_moe(args, tl, synth, dev, world, rank, local):
@@ -384,7 +455,7 @@ def run_moe(args, tl, synth, dev, world, rank, local):
         ms, e2e_ms = t.tolist()
     G = T * topk
     flops = 2.0 * G * (2 * MOE["H"] * MOE["I"] + MOE["I"] * MOE["H"])
-    pk = peaks_tensor()
+    pk = peaks_tensor(ms * args.steps * 1e-3)
     if rank == 0:
         # one GPU: route, gather, 3 grouped GEMMs, combine; expert-parallel: route and
         # gather twice (by owning rank, then by local expert)
@@ -402,7 +473,7 @@ def run_moe(args, tl, synth, dev, world, rank, local):
                 "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": hX.numel() * 2 * world,
                         "d2h_bytes_per_step": hO.numel() * 2 * world},
                 "gpu_launches": launches * args.steps, "clocks": clk.summary(),
-                "cpu_baseline": None}
+                "cpu_baseline": moe_cpu_baseline(m) if world == 1 and not args.no_cpu_baseline else None}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -423,7 +494,7 @@ def run_prefill(args, tl, synth, dev, world, rank, local):
         ms = float(t.item())
     flops = sum(2.0 * PREFILL_M * N * K for K, N in SHAPES)
     value = world * flops / (ms * 1e-3) / 1e12
-    pk = peaks_tensor()
+    pk = peaks_tensor(ms * args.steps * 1e-3)
     if rank == 0:
         line = {"metric": "M=2048 int2 fp16 prefill TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -539,6 +610,293 @@ def run_hadamard(args, tl, synth, dev, world, rank, local):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- C3: s8 x s2 prefill
+# bf16 activations quantised per row and 128-group (ternocl_int8_quant_a), then
+# the s8 x s2 GEMM with int32 accumulation; the quantisation pre-kernel is inside the timed
+# region, as the reference driver times `pre` + `gemm` (int2_via_int2_x_int8_dpas/main.cpp:368-387).
+INT8 = dict(shapes=[(5376, 21504), (21504, 5376), (5376, 5376)], M=2048)
+INT8_METRIC = "M=2048 s8xs2 prefill TFLOP/s (quant_a + GEMM, 27B-like shapes)"
+
+
+def int8_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
+    import torch
+    L = tl.lib()
+    M = INT8["M"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(31)
+    ka = [K * M for K, _ in INT8["shapes"]]
+    kc = [N * M for _, N in INT8["shapes"]]
+    dA = torch.randn(sum(ka), generator=gen, device=dev).bfloat16()
+    dC = torch.empty(sum(kc), dtype=torch.bfloat16, device=dev)
+    oa, oc = np.cumsum([0] + ka), np.cumsum([0] + kc)
+    ly = []
+    for j, (K, N) in enumerate(INT8["shapes"]):
+        ly.append(dict(K=K, N=N, B=device_int2_words(K, N, gen, dev),
+                       SB=(torch.rand(K // 128, N, generator=gen, device=dev) * 0.04 + 0.01).bfloat16(),
+                       A=dA[oa[j]:oa[j + 1]].view(M, K), C=dC[oc[j]:oc[j + 1]].view(M, N),
+                       SA=torch.zeros(K // 128, (M + 31) & ~31, dtype=torch.bfloat16, device=dev),
+                       Aq=torch.empty(M, K, dtype=torch.int8, device=dev)))
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def pre(x):
+        check(tl, "ternocl_int8_quant_a", L.ternocl_int8_quant_a(x["A"].data_ptr(), x["SA"].data_ptr(),
+                                                                x["Aq"].data_ptr(), M, x["K"], 1, sp))
+
+    def gemm(x):
+        check(tl, "ternocl_int2_int8", L.ternocl_int2_int8(x["A"].data_ptr(), x["Aq"].data_ptr(), x["SA"].data_ptr(),
+                                                           x["B"].data_ptr(), x["SB"].data_ptr(), x["C"].data_ptr(),
+                                                           None, None, M, x["N"], x["K"], 1, 0, 0, 0, 0, sp))
+
+    def step():
+        for x in ly:
+            pre(x)
+            gemm(x)
+
+    for _ in range(warmup):
+        step()
+    t_step = time_events(stream, step, steps)
+    t_pre = time_events(stream, lambda: [pre(x) for x in ly], steps)
+    t_gemm = time_events(stream, lambda: [gemm(x) for x in ly], steps)
+    flops = sum(2.0 * M * N * K for K, N in INT8["shapes"])
+    tf, tf_gemm = flops / (t_step * 1e-3) / 1e12, flops / (t_gemm * 1e-3) / 1e12
+    peak, kind = peaks_int8(t_gemm * steps * 1e-3)
+    out = {"metric": INT8_METRIC, "value": tf, "unit": "TFLOP/s", "ms_per_step": t_step, "dtype": "bf16",
+           "config": {"workload": "int2_via_int2_x_int8_dpas prefill (configs[2]): quant_a + s8xs2 GEMM, bf16",
+                      "M": M, "shapes_KxN": INT8["shapes"], "qmode": 0,
+                      "l2": "inputs larger than L2: one step touches ~400 MB (A, Aq, B, C of 3 shapes)"},
+           "pre_ms": t_pre, "gemm_ms": t_gemm,
+           "roofline": {"bound": "tensor", "achieved": tf_gemm, "peak": peak, "unit": "TFLOP/s",
+                        "frac": tf_gemm / peak, "peak_kind": kind, "kernel": "gemm_i8 (tcgen05 kind::i8), GEMM alone",
+                        "traffic": None},
+           "gpu_launches": 2 * len(ly) * steps, "cpu_baseline": None, "e2e": None}
+    if e2e:
+        hA = dA.cpu().pin_memory()
+        hC = torch.empty(dC.shape, dtype=dC.dtype).pin_memory()
+        n = max(3, min(steps, 10))
+        for _ in range(2):
+            dA.copy_(hA, non_blocking=True)
+            step()
+            hC.copy_(dC, non_blocking=True)
+            stream.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            dA.copy_(hA, non_blocking=True)
+            step()
+            hC.copy_(dC, non_blocking=True)
+            stream.synchronize()
+        es = (time.perf_counter() - t0) / n
+        out["e2e"] = {"value": flops / es / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": hA.numel() * 2,
+                      "d2h_bytes_per_step": hC.numel() * 2}
+    if cpu:
+        from oracle import api as orc
+        R = orc.Ref if orc.ref_available() else None
+        rows = 2
+        host = []
+        for x in ly:
+            A = x["A"][:rows].cpu().view(torch.int16).numpy().view(np.uint16)
+            host.append((A, x["B"].cpu().numpy().view(np.uint32), x["SB"].cpu().view(torch.int16).numpy().view(np.uint16),
+                         x["K"], x["N"]))
+
+        def one():
+            for A, B, SB, K, N in host:
+                if R is not None:
+                    SA = R.int8_scale_a(A, rows, K, 1)
+                    R.int8_gold(A, B, SA, SB, rows, K, N, 1)
+                else:
+                    SA = orc.int8_scale_a(A, rows, K, 1)
+                    orc.int8_gold(A, B, SA, SB, rows, K, N, 1)
+
+        nrun, el = cpu_loop(one, 8.0)
+        cflops = nrun * sum(2.0 * rows * N * K for K, N in INT8["shapes"])
+        out["cpu_baseline"] = {"value": cflops / el / 1e12, "unit": "TFLOP/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "kind": "reference" if R is not None else "port",
+                               "sample": "%d passes of compute_scale_a + compute_gold on %d rows of each of the 3 "
+                                         "shapes (M=2048 workload), %.1f s" % (nrun, rows, el)}
+    return out
+
+
+# ----------------------------------------------------------------------------- C4: BITCOS + Hadamard
+# K=5376, N=21504, zero fraction z in {0.2, 0.35, 0.5}, M in {1, 8, 512}, fp16; the
+# activations go through the sign flip + FWHT (HB=256: the config's 1024 does not divide 5376)
+# and then the BITCOS GEMV (M <= 8) or the M-tiled GEMM (M = 512).  Bytes as the reference's
+# model (bitcos_fp16_upcvt/main.cpp:286-300): the BITCOS buffer + scales (+ A and C).
+BITCOS = dict(K=5376, N=21504, z=(0.2, 0.35, 0.5), M=(1, 8, 512), HB=256, sets=3)
+BITCOS_METRIC = "M=1 BITCOS GEMV weight-stream HBM GB/s (Hadamard pre-transform included, K=5376 N=21504)"
+
+
+def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
+    import torch
+    L = tl.lib()
+    K, N, HB = BITCOS["K"], BITCOS["N"], BITCOS["HB"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(41)
+    rng = np.random.default_rng(41)
+    host_bufs, bufs, S = {}, {}, {}
+    for zi, z in enumerate(BITCOS["z"]):
+        host_bufs[z] = [tl.bitcos_random(K, N, z, 100 * zi + k) for k in range(BITCOS["sets"])]
+        bufs[z] = [torch.from_numpy(b.view(np.int32)).to(dev) for b in host_bufs[z]]
+        S[z] = (torch.rand(K // 128, N, generator=gen, device=dev) * 0.04 + 0.01).half()
+    signs_h = np.where(rng.random(K) < 0.5, -1, 1).astype(np.int8)
+    signs = torch.from_numpy(signs_h).to(dev)
+    A = {M: torch.randn(M, K, generator=gen, device=dev).half() for M in BITCOS["M"]}
+    Y = {M: torch.empty(M, K, dtype=torch.float16, device=dev) for M in BITCOS["M"]}
+    C = {M: torch.empty(M, N, dtype=torch.float16, device=dev) for M in BITCOS["M"]}
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def had(M):
+        check(tl, "ternocl_hadamard_fwht", L.ternocl_hadamard_fwht(A[M].data_ptr(), signs.data_ptr(), Y[M].data_ptr(),
+                                                                   M, K, HB, 1, 0, sp))
+
+    def gemv(M, z, i):
+        check(tl, "ternocl_bitcos_upcvt", L.ternocl_bitcos_upcvt(Y[M].data_ptr(), bufs[z][i].data_ptr(),
+                                                                 S[z].data_ptr(), None, 1, C[M].data_ptr(), None,
+                                                                 None, M, N, K, 0, 0, 0, 0, sp))
+
+    per = []
+    for M in BITCOS["M"]:
+        for z in BITCOS["z"]:
+            ctr = [0]
+
+            def pipeline(M=M, z=z):
+                had(M)
+                gemv(M, z, ctr[0] % BITCOS["sets"])
+                ctr[0] += 1
+
+            def alone(M=M, z=z):
+                gemv(M, z, ctr[0] % BITCOS["sets"])
+                ctr[0] += 1
+
+            reps = steps if M < 512 else max(3, steps // 10)
+            for _ in range(warmup):
+                pipeline()
+            t_pipe = time_events(stream, pipeline, reps)
+            t_gemv = time_events(stream, alone, reps)
+            wbytes = host_bufs[z][0].size * 4 + (K // 128) * N * 2
+            per.append(dict(M=M, z=z, us_per_call=t_pipe * 1e3, gemv_us=t_gemv * 1e3, weight_bytes=wbytes,
+                            GBps=wbytes / (t_pipe * 1e-3) / 1e9 if M <= 8 else None,
+                            TFLOPs=2.0 * M * N * K / (t_pipe * 1e-3) / 1e12))
+    m1 = [q for q in per if q["M"] == 1]
+    value = sum(q["weight_bytes"] for q in m1) / (sum(q["us_per_call"] for q in m1) * 1e-6) / 1e9
+    mid = [q for q in m1 if q["z"] == 0.35][0]
+    ach = mid["weight_bytes"] / (mid["gemv_us"] * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+    out = {"metric": BITCOS_METRIC, "value": value, "unit": "GB/s", "ms_per_step": sum(q["us_per_call"] for q in m1) / 1e3,
+           "dtype": "fp16",
+           "config": {"workload": "bitcos_fp16_upcvt + hadamard_fwht (configs[3])", "K": K, "N": N, "HB": HB,
+                      "z": list(BITCOS["z"]), "M": list(BITCOS["M"]),
+                      "l2": "inputs larger than L2: %d BITCOS buffers (~%d MB) rotated per call" % (
+                          len(BITCOS["z"]) * BITCOS["sets"], sum(b.size * 4 for z in BITCOS["z"] for b in host_bufs[z]) >> 20),
+                      "per_call": per},
+           "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                        "peak_kind": peak_kind, "kernel": "bitcos GEMV, M=1, z=0.35 (alone)", "traffic": None},
+           "gpu_launches": 2 * steps * len(m1), "cpu_baseline": None, "e2e": None}
+    if e2e:
+        hA = A[1].cpu().pin_memory()
+        hC = torch.empty(1, N, dtype=torch.float16).pin_memory()
+        n, tot, t0 = 0, 0.0, time.perf_counter()
+        for it in range(steps):
+            for z in BITCOS["z"]:
+                A[1].copy_(hA, non_blocking=True)
+                had(1)
+                gemv(1, z, it % BITCOS["sets"])
+                hC.copy_(C[1], non_blocking=True)
+                stream.synchronize()
+                tot += host_bufs[z][0].size * 4 + (K // 128) * N * 2
+        es = time.perf_counter() - t0
+        out["e2e"] = {"value": tot / es / 1e9, "unit": "GB/s", "h2d_bytes_per_step": hA.numel() * 2 * len(BITCOS["z"]),
+                      "d2h_bytes_per_step": hC.numel() * 2 * len(BITCOS["z"])}
+    if cpu:
+        from oracle import api as orc
+        R = orc.Ref if orc.ref_available() else None
+        Ah = A[1].cpu().view(torch.int16).numpy().view(np.uint16)
+        Sh = {z: S[z].cpu().view(torch.int16).numpy().view(np.uint16) for z in BITCOS["z"]}
+
+        def one():
+            for z in BITCOS["z"]:
+                if R is not None:
+                    y = R.hadamard(Ah, signs_h, 1, K, HB, 1, 0)
+                    R.bitcos_gold(y, host_bufs[z][0], Sh[z], 1, K, N, 0)
+                else:
+                    y = orc.hadamard(Ah, signs_h, 1, K, HB, 1, 0)
+                    orc.bitcos_gold(y, host_bufs[z][0], Sh[z], 1, K, N, 0)
+
+        nrun, el = cpu_loop(one, 8.0)
+        cb = nrun * sum(host_bufs[z][0].size * 4 + (K // 128) * N * 2 for z in BITCOS["z"])
+        out["cpu_baseline"] = {"value": cb / el / 1e9, "unit": "GB/s",
+                               "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                               "kind": "reference" if R is not None else "port",
+                               "sample": "%d passes of the hadamard_fwht kernel source run on the CPU + the BITCOS "
+                                         "compute_gold at M=1 over the three z, %.1f s" % (nrun, el)}
+    return out
+
+
+def moe_cpu_baseline(m, budget_s=8.0):
+    """The MoE layer's token reference (int2_moe/prefill.cpp:291-310, double precision; the
+    restatement, pinned through its parts) on the host cores: tokens/s over a bounded
+    number of tokens of the same workload."""
+    import torch
+    from oracle import api as orc
+
+    def h16(t):
+        return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+    def h32(t):
+        return t.cpu().numpy().view(np.uint32)
+
+    X, RW, ids = h16(m["X"]), h16(m["RW"]), m["ids"].cpu().numpy()
+    W = [h32(m["Bg"]), h16(m["Sg"]), h32(m["Bu"]), h16(m["Su"]), h32(m["Bd"]), h16(m["Sd"])]
+    tok = [0]
+
+    def one():
+        orc.moe_token_ref(X, ids, RW, *W, tok[0] % MOE["T"], MOE["topk"], MOE["H"], MOE["I"], 0)
+        tok[0] += 1
+
+    n, el = cpu_loop(one, budget_s)
+    return {"value": n / el, "unit": "tokens/s", "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+            "kind": "port", "sample": "%d tokens of the double-precision token reference, %.1f s" % (n, el)}
+
+
+def emit(args, line, clocks, world=1):
+    """Prints a secondary measurement as its own JSON line (--workload int8 / bitcos)."""
+    full = {"metric": line["metric"], "value": line["value"], "unit": line["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": line["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": line["dtype"], "data": "synthetic",
+            "config": dict(line["config"], parallelism="replicas x%d" % world if world > 1 else "single GPU"),
+            "roofline": line["roofline"], "e2e": line["e2e"], "gpu_launches": line["gpu_launches"],
+            "clocks": clocks, "cpu_baseline": line["cpu_baseline"]}
+    for k in ("pre_ms", "gemm_ms"):
+        if k in line:
+            full[k] = line[k]
+    print(json.dumps(full), flush=True)
+
+
+def run_replicated(args, tl, dev, world, rank, local):
+    """--workload int8 / bitcos: configs[2] / configs[3] as the line; N GPUs run replicas
+    (weak scaling), the time per step is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+    fn = int8_measure if args.workload == "int8" else bitcos_measure
+    cpu = world == 1 and not args.no_cpu_baseline
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        line = fn(tl, dev, args.steps, args.warmup, cpu=cpu, e2e=True)
+    if world > 1:
+        t = torch.tensor([line["ms_per_step"]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        scale = line["ms_per_step"] / float(t.item())
+        line["value"] *= world * scale
+        line["ms_per_step"] = float(t.item())
+    if rank == 0:
+        emit(args, line, clk.summary(), world)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -550,10 +908,11 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "moe", "hadamard"],
-                    help="decode: the headline M=1 GEMV sweep (+ prefill and MoE as secondary figures); "
-                         "prefill: the M=2048 GEMMs alone; moe: the MoE prefill layer (expert-parallel on N GPUs); "
-                         "hadamard: the sign flip + FWHT of the BITCOS config")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "int8", "bitcos", "moe", "hadamard"],
+                    help="decode: the headline M=1 GEMV sweep (+ the other configs as secondary figures); "
+                         "prefill: the int2 fp16 M=2048 GEMMs on the 8B shapes; int8: the s8xs2 prefill of configs[2] "
+                         "(quant_a + GEMM); bitcos: configs[3], Hadamard + BITCOS GEMV/GEMM; moe: the MoE prefill "
+                         "layer (expert-parallel on N GPUs); hadamard: the sign flip + FWHT of the BITCOS config")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="N>1: GEMV + NCCL all-gather instead of the GEMV with the all-gather fused in its epilogue")
@@ -590,6 +949,8 @@ def main():
         return run_moe(args, tl, synth, dev, world, rank, local)
     if args.workload == "hadamard":
         return run_hadamard(args, tl, synth, dev, world, rank, local)
+    if args.workload in ("int8", "bitcos"):
+        return run_replicated(args, tl, dev, world, rank, local)
 
     # per-rank column slices (multiples of 16)
     def cols(N):
@@ -782,13 +1143,18 @@ def main():
     secondary = None
     if world == 1 and not args.no_secondary:
         tf, pms, _ = prefill_measure(tl, synth, dev, steps=min(args.steps, 20), warmup=3)
-        pk = pk_moe = peaks_tensor()
-        mt, mtf, mms = moe_measure(tl, synth, dev, steps=min(args.steps, 10), warmup=2)
+        pk = peaks_tensor(pms * min(args.steps, 20) * 1e-3)
+        pk_moe = peaks_tensor(mms * min(args.steps, 10) * 1e-3)
+        mt, mtf, mms, me2e, mcpu = moe_measure(tl, synth, dev, steps=min(args.steps, 10), warmup=2,
+                                               cpu=not args.no_cpu_baseline)
         secondary_moe = {"metric": "MoE prefill tokens/s (T=4096, H=2048, I=768, E=128, top-8, fp16)", "value": mt,
                          "unit": "tokens/s", "ms_per_layer": mms, "tflops": mtf,
                          "roofline": {"bound": "tensor", "achieved": mtf, "peak": pk_moe[0], "unit": "TFLOP/s",
-                                      "frac": mtf / pk_moe[0], "peak_kind": pk_moe[1]}}
-        secondary = {"moe": secondary_moe,
+                                      "frac": mtf / pk_moe[0], "peak_kind": pk_moe[1]},
+                         "e2e": me2e, "cpu_baseline": mcpu}
+        sec_int8 = int8_measure(tl, dev, steps=min(args.steps, 20), warmup=3, cpu=not args.no_cpu_baseline)
+        sec_bitcos = bitcos_measure(tl, dev, steps=min(args.steps, 50), warmup=3, cpu=not args.no_cpu_baseline)
+        secondary = {"int8_prefill": sec_int8, "bitcos": sec_bitcos, "moe": secondary_moe,
                      "prefill": {"metric": "M=2048 int2 fp16 prefill TFLOP/s (tcgen05 GEMM)", "value": tf,
                                  "unit": "TFLOP/s", "ms_per_step": pms, "M": PREFILL_M, "shapes_KxN": SHAPES,
                                  "roofline": {"bound": "tensor", "achieved": tf, "peak": pk[0], "unit": "TFLOP/s",

@@ -94,9 +94,16 @@ int ternocl_device_error(int reset);
  *    measured faster for the longer ones).
  *  TERNOCL_OPT_GEMV_IMPL (default 0 = chosen per M): the int2 decode GEMV used by
  *    ternocl_int2_upcvt at small M: 1 = fp16/bf16 MMA on decoded weights, 2 = integer
- *    MMA on int8 weights and exact fixed-point activations (M <= 4, the default there),
- *    3 = the same arithmetic in a persistent kernel fed by TMA with a stream-K split
- *    (M = 1; measured slower than 2 on B200, so opt-in).
+ *    MMA on int8 weights and exact fixed-point activations, one CTA per 32-column strip
+ *    (M <= 4; the default there when no workspace is given), 3 = the same arithmetic in a
+ *    persistent kernel fed by TMA with a stream-K split (M = 1; opt-in), 4 = the same
+ *    arithmetic in one balanced wave of one CTA per SM, each warp streaming a contiguous
+ *    range of (strip, 128-row group) units (M <= 4 with a workspace; the default there).
+ *  TERNOCL_OPT_GEMV_STAGES (default 0 = planned): units (1 KB of weights each) in flight
+ *    per warp in the stream-K GEMV of GEMV_IMPL 4: 4, 6 or 8.
+ *  TERNOCL_OPT_PEER_TIMEOUT_MS (default 2000, 1..60000): how long the column-sharded GEMV
+ *    (ternocl_int2_upcvt_allgather) waits for its peers before it gives up, sets bit 2 of
+ *    ternocl_device_error and returns.
  * Returns the previous value, or -1 for an unknown option or value. */
 typedef enum {
     TERNOCL_OPT_PDL = 1,
@@ -104,7 +111,9 @@ typedef enum {
     TERNOCL_OPT_GEMV_SPLIT = 3,
     TERNOCL_OPT_GEMV_WARPS = 4,
     TERNOCL_OPT_GEMM_PERSISTENT = 5,
-    TERNOCL_OPT_GEMV_IMPL = 6
+    TERNOCL_OPT_GEMV_IMPL = 6,
+    TERNOCL_OPT_GEMV_STAGES = 7,
+    TERNOCL_OPT_PEER_TIMEOUT_MS = 8
 } ternocl_option;
 int ternocl_set_option(int option, int value);
 
@@ -136,12 +145,16 @@ int ternocl_int2_upcvt(const void *A, const uint32_t *B, const void *S, void *C,
  * this computes the same C as ternocl_int2_upcvt (same arguments and rules, no
  * workspace argument) and takes its split-K scratch from a 16 MiB array the library
  * declares in device memory, which every GPU that loads the library holds until exit.
- *  - Shapes whose scratch (2 x M x N fp32 partial sums + counters) exceeds 16 MiB
- *    are rejected with TERNOCL_ERR_WORKSPACE.
+ *  - It runs the plan ternocl_int2_upcvt makes for a 16 MiB workspace (same kernel,
+ *    warps and K split, bit-identical output).  A shape whose plan would need more
+ *    scratch runs in the forms that need none; a shape that no form can run is
+ *    rejected with TERNOCL_ERR_WORKSPACE.
  *  - The first call on a device looks up the array's address (cudaGetSymbolAddress,
- *    that device current); make that first call before any stream capture.
- *  - All calls share the array: the counters are cleared on `stream` before each
- *    launch; calls that overlap on the GPU race on it.
+ *    that device current) and keeps it; make that first call before any stream
+ *    capture.  Resetting the device (cudaDeviceReset) while the library stays loaded
+ *    is not supported.
+ *  - All calls share the array: the arrival counters are cleared on `stream` before
+ *    each launch; calls that overlap on the GPU race on it.
  *  - Calls no cudaMalloc, cudaFree or allocating library routine. */
 int ternocl_int2_upcvt_noalloc(const void *A, const uint32_t *B, const void *S, void *C,
                                const void *Other, const void *Bias, int M, int N, int K, int dtype,
@@ -155,12 +168,16 @@ int ternocl_int2_upcvt_noalloc(const void *A, const uint32_t *B, const void *S, 
  * in this process, e.g. CUDA IPC mappings of the peers' buffers; Other [M, N] and Bias
  * [N] are full width).  The launch completes only after all ranks' columns have
  * arrived: the grid's last CTA writes `epoch` into flags_ranks[r][rank] of every rank and
- * waits until flags_ranks[rank][r] >= epoch for all r (bounded to ~2 s; a timeout sets
- * bit 2 of ternocl_device_error).  flags start at 0 and `epoch` must increase by one per
+ * waits until flags_ranks[rank][r] >= epoch for all r (bounded; a timeout sets bit 2 of
+ * ternocl_device_error).  flags start at 0 and a nonzero `epoch` must increase by one per
  * call, in the same order on every rank.  A rank must not read a C buffer after it has
  * launched the next call that writes it (double-buffer C if the output is consumed across
- * calls).  ws: >= ternocl_gemv_allgather_workspace_size(M, nl, K) bytes, zeroed once,
- * 256-byte aligned. */
+ * calls).  epoch == 0: the library counts the calls itself, on the device, in
+ * flags_ranks[rank][world] (each rank's flag array then has world + 1 entries, all zero
+ * at the start); no host value changes from call to call, so the call can be captured in
+ * a CUDA graph and replayed, on every rank in the same order.  The wait for the peers is
+ * bounded by TERNOCL_OPT_PEER_TIMEOUT_MS.  ws: >= ternocl_gemv_allgather_workspace_size(M,
+ * nl, K) bytes, zeroed once, 256-byte aligned. */
 size_t ternocl_gemv_allgather_workspace_size(int M, int nl, int K);
 /* CUDA IPC helpers to map the peers' C and flag buffers (set-up time, not the hot path;
  * plain peer mappings, no multicast objects): the 64-byte handle and byte offset of a

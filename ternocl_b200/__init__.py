@@ -18,6 +18,8 @@ OPT_GEMV_SPLIT = 3
 OPT_GEMV_WARPS = 4
 OPT_GEMM_PERSISTENT = 5
 OPT_GEMV_IMPL = 6
+OPT_GEMV_STAGES = 7
+OPT_PEER_TIMEOUT_MS = 8
 
 
 def _torch():

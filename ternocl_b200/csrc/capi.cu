@@ -56,6 +56,9 @@ static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // shared memory a GEMV CTA may use (activation staging + weight ring)
 constexpr size_t kGemvSmemBudget = 100 * 1024;
+// shared memory of a one-CTA-per-SM GEMV that leaves room on the SM for the next
+// kernel's CTA of the same size (228 KB per SM, 1 KB reserved per CTA)
+constexpr size_t kGemvCoresidentSmem = 112 * 1024;
 constexpr int kMaxClusterSK = 8;  // portable thread-block cluster size
 
 // Split-K plan of a decode GEMV whose CTAs cover `cols` columns x `rows` activation
@@ -244,6 +247,23 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
         return cuda_status(int2_gemv_p_launch(a));
     }
     const bool digit = M <= kGemvDigitMaxM && impl != 1;
+    if (digit && !peer && ws && (impl == 0 || impl == 4)) {
+        // stream-K integer-MMA GEMV: one balanced wave; small enough (<= ~110 KB of shared
+        // memory) that the next GEMV of the stream fits beside it on every SM
+        const int ctas = int2_gemv_s_ctas(M, N, K, sm_count());
+        int depth = options().gemv_stages;
+        if (!depth) {
+            depth = 8;
+            while (depth > 4 && int2_gemv_s_smem(M, K, depth) > kGemvCoresidentSmem) depth -= 2;
+        }
+        if (ctas >= 1 && int2_gemv_s_smem(M, K, depth) <= 227 * 1024 &&
+            int2_gemv_s_workspace(M, N, ctas) <= ws_bytes) {
+            if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
+            a.ws_cnt = (unsigned *)ws;
+            a.ws_part = (float *)((char *)ws + int2_gemv_s_cnt_bytes(N));
+            return cuda_status(int2_gemv_s_launch(a, ctas, depth));
+        }
+    }
     auto plan = [&](bool allow_ws) { return digit ? gemv_digit_plan(M, N, K, allow_ws) : gemv_plan(M, N, K, allow_ws); };
     GemvPlan p = plan(ws != nullptr);
     if (p.total() > ws_bytes) p = plan(false);
@@ -260,6 +280,13 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
     return cuda_status(digit ? int2_gemv_d_launch(a) : int2_gemv_launch(a));
 }
 int report_cuda(cudaError_t e) { return cuda_status(e); }
+
+size_t int2_gemv_counter_bytes(int M, int N) {
+    // per-strip kernels: one counter per (32-column strip, row block of >= 4 rows);
+    // stream-K: one per strip
+    const size_t tiles = (size_t)((N + 31) / 32) * (size_t)((M + 3) / 4);
+    return round_up(tiles * sizeof(unsigned), 256);
+}
 
 // (kernel, device) -> dynamic shared memory attribute already set
 namespace {
@@ -342,9 +369,21 @@ int ternocl_set_option(int option, int value) {
         return old;
     }
     if (option == TERNOCL_OPT_GEMV_IMPL) {
-        if (value < 0 || value > 3) return -1;
+        if (value < 0 || value > 4) return -1;
         const int old = options().gemv_impl;
         options().gemv_impl = value;
+        return old;
+    }
+    if (option == TERNOCL_OPT_GEMV_STAGES) {
+        if (value != 0 && value != 4 && value != 6 && value != 8) return -1;
+        const int old = options().gemv_stages;
+        options().gemv_stages = value;
+        return old;
+    }
+    if (option == TERNOCL_OPT_PEER_TIMEOUT_MS) {
+        if (value < 1 || value > 60000) return -1;
+        const int old = options().peer_timeout_ms;
+        options().peer_timeout_ms = value;
         return old;
     }
     if (option == TERNOCL_OPT_GEMM_TILE_M) {
@@ -365,6 +404,10 @@ size_t ternocl_gemv_workspace_size(int M, int N, int K) {
     if (b > need) need = b;
     if (c > need) need = c;
     if (M == 1 && int2_gemv_p_workspace(N) > need) need = int2_gemv_p_workspace(N);
+    if (M <= kGemvDigitMaxM) {
+        const size_t s = int2_gemv_s_workspace(M, N, int2_gemv_s_ctas(M, N, K, sm_count()));
+        if (s > need) need = s;
+    }
     return need;
 }
 

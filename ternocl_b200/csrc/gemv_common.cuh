@@ -66,7 +66,8 @@ struct Params {
     // C with N_out columns and stores them into every rank's copy C_peer[r]; Other and
     // Bias are the full-width arrays.  flag_peer[r] = rank r's flags (one per rank).
     int world, rank, n_off, N_out;
-    unsigned epoch;
+    unsigned epoch;               // 0: kept on the device in flag_peer[rank][world]
+    unsigned long long peer_timeout_ns;
     unsigned *done_cnt;
     unsigned *err;  // device error word of the launching library (bit 2: a peer wait timed out)
     void *C_peer[kMaxPeers];
@@ -129,6 +130,7 @@ inline Params gemv_params_impl(const GemvArgs &a) {
     p.n_off = a.n_off;
     p.N_out = a.N_out;
     p.epoch = a.epoch;
+    p.peer_timeout_ns = (unsigned long long)options().peer_timeout_ms * 1000000ull;
     p.done_cnt = a.done_cnt;
     p.err = a.err;
     for (int r = 0; r < kMaxPeers; ++r) {
@@ -334,10 +336,14 @@ __device__ __forceinline__ uint64_t gtimer_ns() {
 }
 
 // Column-sharded completion: every CTA counts itself once its peer stores are fenced;
-// the last CTA of the grid writes `epoch` into its slot of every rank's flags and waits
-// until every rank has written `epoch` into this rank's flags, so the launch completes
-// only when the whole of C has arrived.  The wait gives up after ~2 s (error word bit 2).
-__device__ __forceinline__ void peer_complete(const Params &p, unsigned *err) {
+// the last CTA of the grid writes the call's epoch into its slot of every rank's flags
+// and waits until every rank has written that epoch into this rank's flags, so the
+// launch completes only when the whole of C has arrived.  With p.epoch == 0 the epoch is
+// the rank's own call count, kept in flag_peer[rank][world] and bumped here (the same
+// sequence on every rank, and no host value in the launch: a graph replays it).  The
+// wait gives up after p.peer_timeout_ns (error word bit 2) and the kernel returns.
+template <class P>
+__device__ __forceinline__ void peer_complete(const P &p, unsigned *err) {
     __syncthreads();
     if (threadIdx.x != 0) return;
     __threadfence_system();
@@ -345,13 +351,19 @@ __device__ __forceinline__ void peer_complete(const Params &p, unsigned *err) {
     if (atomicAdd(p.done_cnt, 1u) != total - 1) return;
     *p.done_cnt = 0u;  // ready for the next launch
     __threadfence_system();
-    for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_peer[r] + p.rank, p.epoch);
+    unsigned epoch = p.epoch;
+    if (epoch == 0u) {
+        unsigned *count = p.flag_peer[p.rank] + p.world;
+        epoch = *count + 1u;
+        *count = epoch;
+    }
+    for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_peer[r] + p.rank, epoch);
     const unsigned *mine = p.flag_peer[p.rank];
     const uint64_t t0 = gtimer_ns();
     for (int r = 0; r < p.world; ++r) {
         uint32_t i = 0;
-        while ((int)(ld_acquire_sys(mine + r) - p.epoch) < 0) {
-            if ((++i & 255u) == 0 && gtimer_ns() - t0 > 2000000000ull) {
+        while ((int)(ld_acquire_sys(mine + r) - epoch) < 0) {
+            if ((++i & 255u) == 0 && gtimer_ns() - t0 > p.peer_timeout_ns) {
                 atomicOr(err, 4u);
                 return;
             }

@@ -12,7 +12,12 @@
 //    library until the process exits;
 //  * the first call on a device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it, so that first
-//    call should come before any stream capture;
+//    call should come before any stream capture; the cached address belongs to the
+//    device's context of that moment, so resetting the device (cudaDeviceReset) while
+//    the library stays loaded is not supported;
+//  * the GEMV is the one ternocl_int2_upcvt plans for a workspace of the array's size
+//    (with the same kernel, warps and split); shapes whose plan would need more scratch
+//    run in the forms that need none, and only shapes no form can run are refused;
 //  * every call shares the array and it keeps the last call's contents: the arrival
 //    counters are cleared on the stream (cudaMemsetAsync) before each launch, and
 //    calls that overlap on the GPU (e.g. on two streams) race on it;
@@ -60,45 +65,27 @@ using namespace ternocl;
 extern "C" int ternocl_int2_upcvt_noalloc(const void *A, const uint32_t *B, const void *S, void *C,
                                           const void *Other, const void *Bias, int M, int N, int K,
                                           int dtype, int postop, int out_f32, void *stream) {
-    // same argument rules as ternocl_int2_upcvt
+    // same argument rules as ternocl_int2_upcvt (checked again by the planner below)
     if (dtype != TERNOCL_FP16 && dtype != TERNOCL_BF16) return TERNOCL_ERR_ARG;
     if (postop < 0 || postop > 4 || (out_f32 != 0 && out_f32 != 1)) return TERNOCL_ERR_ARG;
     if (M < 0 || N <= 0 || K <= 0 || N % 16 || K % kGS) return TERNOCL_ERR_SHAPE;
     if (!A || !B || !S || !C) return TERNOCL_ERR_ARG;
-    if ((postop == 1 || postop == 2) && !Other) return TERNOCL_ERR_ARG;
-    if (postop == 3 && !Bias) return TERNOCL_ERR_ARG;
-    auto al = [](const void *p, size_t a) { return ((uintptr_t)p % a) == 0; };
-    if (!al(A, 16) || !al(B, 16) || !al(S, 16) || !al(C, out_f32 ? 16 : 8)) return TERNOCL_ERR_ARG;
-    if ((Other && !al(Other, 8)) || (Bias && !al(Bias, out_f32 ? 8 : 4))) return TERNOCL_ERR_ARG;
     if (M == 0) return TERNOCL_OK;
 
-    // split-K through the scratch array: as many splits as the GEMV's own plan
-    // wants (>= 2 when K has two scale groups), as long as the partials fit
-    const int G = K / kGS;
-    const size_t tiles = (size_t)((N + 31) / 32) * (size_t)((M + 7) / 8);
-    const size_t cnt_bytes = (tiles * sizeof(unsigned) + 255) / 256 * 256;
-    int sk = gemv_split_k(M, N, K);
-    if (sk < 2) sk = 2;
-    if (sk > G) sk = G;
-    auto need = [&](int s) { return cnt_bytes + (size_t)s * M * N * sizeof(float); };
-    while (sk > 2 && need(sk) > kNoAllocScratchBytes) --sk;
-    if (sk >= 2 && need(sk) > kNoAllocScratchBytes) return TERNOCL_ERR_WORKSPACE;  // M*N too large
-    if (int2_gemv_smem(M, K, sk) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
-
-    GemvArgs a;
-    a.A = A; a.B = B; a.S = S; a.C = C; a.Other = Other; a.Bias = Bias;
-    a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
-    a.stream = (cudaStream_t)stream;
-    a.SK = sk < 1 ? 1 : sk;
-    a.cluster = 0;
-    if (a.SK > 1) {
-        void *scratch = nullptr;
-        cudaError_t e = scratch_ptr(&scratch);
-        if (e != cudaSuccess) return report_cuda(e);
-        a.ws_cnt = (unsigned *)scratch;
-        a.ws_part = (float *)((char *)scratch + cnt_bytes);
-        e = cudaMemsetAsync(scratch, 0, cnt_bytes, a.stream);  // counters start at zero
-        if (e != cudaSuccess) return report_cuda(e);
-    }
-    return report_cuda(int2_gemv_launch(a));
+    // The GEMV runs exactly as ternocl_int2_upcvt plans it for a workspace of the
+    // array's size: the stream-K kernel or the per-strip kernels, with the split the
+    // plan picks (none where it picks none).  A plan whose scratch would not fit the
+    // array falls back to the forms that need none; a shape no form can run is refused.
+    void *scratch = nullptr;
+    cudaError_t e = scratch_ptr(&scratch);
+    if (e != cudaSuccess) return report_cuda(e);
+    // The arrival counters at the start of the array must be zero when a call begins.
+    // Every completed call leaves them zero, but a call cut short (a failed launch, a
+    // killed process sharing nothing else) could not; clear them on the stream.
+    const size_t cnt = int2_gemv_counter_bytes(M, N);
+    if (cnt > kNoAllocScratchBytes) return TERNOCL_ERR_WORKSPACE;
+    e = cudaMemsetAsync(scratch, 0, cnt, (cudaStream_t)stream);
+    if (e != cudaSuccess) return report_cuda(e);
+    return plan_and_launch_int2_gemv(A, B, S, C, Other, Bias, M, N, K, dtype, postop, out_f32, scratch,
+                                     kNoAllocScratchBytes, stream, nullptr);
 }

@@ -77,7 +77,9 @@ class FusedAllGatherGemv:
     """Column-sharded int2 GEMV whose epilogue writes this rank's columns into every
     rank's C (ternocl_int2_upcvt_allgather): C [M, N] is complete on every rank when the
     launch finishes, with no separate collective.  Two C buffers alternate between calls
-    so a rank may read the previous output while the next call is being written."""
+    so a rank may read the previous output while the next call is being written.  The
+    call count that orders the ranks' handshakes is kept on the device (epoch 0), so a
+    sequence of calls can be captured in a CUDA graph and replayed on every rank."""
 
     def __init__(self, M, N, K, dtype, device, group=None):
         import ctypes
@@ -89,7 +91,8 @@ class FusedAllGatherGemv:
         self.n0, self.nl = column_shard(N, self.world, self.rank)
         self.dt = dtype_code(torch.empty(0, dtype=dtype))
         self.C = [torch.empty(M, N, dtype=dtype, device=device) for _ in range(2)]
-        self.flags = torch.zeros(self.world, dtype=torch.int32, device=device)
+        # one flag per rank + this rank's call count (the device-kept epoch)
+        self.flags = torch.zeros(self.world + 1, dtype=torch.int32, device=device)
         self.ws = torch.zeros(lib().ternocl_gemv_allgather_workspace_size(M, self.nl, K), dtype=torch.uint8,
                               device=device)
         self._mapped = []
@@ -101,17 +104,17 @@ class FusedAllGatherGemv:
         fptrs, mapped = ipc_peers(self.flags, group)
         self.f_ptrs = (ctypes.c_void_p * self.world)(*fptrs)
         self._mapped += mapped
-        self.epoch = 0
+        self.calls = 0
         dist.barrier(group=group)
 
     def __call__(self, A, B_shard, S_shard, postop=0, other=None, bias=None, stream=None):
         """A [M, K]; B_shard [K/16, nl], S_shard [K/128, nl] = this rank's columns.  Returns C."""
         from . import _ptr, _stream, call
-        self.epoch += 1
-        buf = self.epoch & 1
+        self.calls += 1
+        buf = self.calls & 1
         call("ternocl_int2_upcvt_allgather", _ptr(A), _ptr(B_shard), _ptr(S_shard), self.c_ptrs[buf], _ptr(other),
              _ptr(bias), self.M, self.N, self.n0, self.nl, self.K, self.dt, int(postop), 0, self.rank, self.world,
-             self.f_ptrs, self.epoch, self.ws.data_ptr(), self.ws.numel(), _stream(stream))
+             self.f_ptrs, 0, self.ws.data_ptr(), self.ws.numel(), _stream(stream))
         return self.C[buf]
 
     def close(self):

@@ -110,3 +110,30 @@ def gemv_worker(rank, world, port, outdir):
     torch.save(C, os.path.join(outdir, "gemv_%d.pt" % rank))
     dist.barrier()
     dist.destroy_process_group()
+
+
+def absent_rank_worker(rank, world, port, tmp):
+    """Rank 1 joins the group and then leaves without taking part in the step (it never
+    arrives at the all-gather of the sharded GEMV); rank 0's collective must end with an
+    error within the group's short timeout instead of waiting for ever."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    dist.barrier()
+    if rank != 0:
+        return  # leaves between steps: nothing of it is in flight
+    rng = np.random.default_rng(11)
+    M, K, N = 3, 512, 272
+    A = torch.from_numpy(synth.activations(rng, M, K, 0).view(np.float16))
+    B = torch.from_numpy(synth.pack_int2(synth.ternary(rng, K, N)).view(np.int32))
+    S = torch.from_numpy(synth.scales(rng, K, N, 0).view(np.float16))
+    n0, nl = tdist.column_shard(N, world, rank)
+    t0 = time.perf_counter()
+    outcome = "completed"
+    try:
+        tdist.sharded_upcvt(A, B[:, n0:n0 + nl].contiguous(), S[:, n0:n0 + nl].contiguous(), N, upcvt=cpu_upcvt)
+    except Exception as e:  # gloo: timeout, or the peer's connection closed
+        outcome = "error: " + type(e).__name__
+    torch.save({"outcome": outcome, "seconds": time.perf_counter() - t0}, os.path.join(tmp, "absent_0.pt"))

@@ -54,3 +54,12 @@ def test_expert_parallel_moe_matches_single_rank(workers, tmp_path):
                                   kernels=workers.CpuKernels())(p["X"], p["ids"], p["RW"])
     assert O.shape == ref.shape
     assert torch.allclose(O.float(), ref.float(), rtol=2e-3, atol=1e-3)
+
+
+def test_absent_rank_ends_the_collective_with_an_error(workers, tmp_path):
+    # failure detection on the host: a rank that never arrives makes the other rank's next
+    # collective fail within the process group's timeout (3 s), no hang
+    spawn(workers.absent_rank_worker, 2, tmp_path)
+    d = torch.load(tmp_path / "absent_0.pt")
+    assert d["outcome"].startswith("error"), d
+    assert d["seconds"] < 30.0, d

@@ -27,16 +27,17 @@ def run(tl, c, M, K, N, bf16, postop, out_f32, algo, ws=None):
 
 
 # GEMV implementations: fp16/bf16 mma.sync on decoded weights, integer mma.sync on int8
-# weights and fixed-point activation digits (M <= 4), the persistent TMA-fed variant of
-# the latter (M = 1; larger M fall back), tcgen05/TMEM
-ALGOS = ["f16", "digit", "persist", "tmem"]
+# weights and fixed-point activation digits (M <= 4) per 32-column strip, the same as one
+# balanced stream-K wave (M <= 4 with a workspace), the persistent TMA-fed variant
+# (M = 1; larger M fall back), tcgen05/TMEM
+ALGOS = ["f16", "digit", "stream", "persist", "tmem"]
 
 
 @pytest.fixture
 def gemv_algo(request, tl):
     """Maps an ALGOS name to (algo argument, implementation option) for the test body."""
     def select(name):
-        impl = {"f16": 1, "digit": 2, "persist": 3, "tmem": 0}[name]
+        impl = {"f16": 1, "digit": 2, "stream": 4, "persist": 3, "tmem": 0}[name]
         old = tl.set_option(tl.OPT_GEMV_IMPL, impl)
         request.addfinalizer(lambda: tl.set_option(tl.OPT_GEMV_IMPL, old))
         return tl.ALGO_GEMV_TMEM if name == "tmem" else tl.ALGO_GEMV
@@ -121,32 +122,35 @@ def test_decode_bit_exact(cuda, tl, gemv_algo, algo):
     assert np.array_equal(out, np.array([0, 1, -2, -1], np.float32)[codes])
 
 
-def test_digit_onehot_bit_exact(cuda, tl, gemv_algo):
-    # the integer-MMA GEMV at M = 4 with one-hot activation rows: C[i, n] is the decoded
-    # weight of row k_i exactly (every code and every position of a 16-row word)
+@pytest.mark.parametrize("impl", ["digit", "stream"])
+def test_digit_onehot_bit_exact(cuda, tl, gemv_algo, impl):
+    # the integer-MMA GEMVs at M = 4 with one-hot activation rows: C[i, n] is the decoded
+    # weight of row k_i exactly (every code and every position of a 16-row word); the
+    # stream-K shape gives every warp one unit, so every strip is summed from 8 pieces
     from ternocl_b200 import synth
-    algo = gemv_algo("digit")
-    K, N = 256, 64
+    algo = gemv_algo(impl)
+    K, N = (256, 64) if impl == "digit" else (1024, 256)
     rng = np.random.default_rng(18)
     B = rng.integers(0, 1 << 32, size=(K // 16, N), dtype=np.uint64).astype(np.uint32)
     S = synth.to_dt(np.ones((K // 128, N)), 0)
     k = np.arange(K)[:, None]
     codes = (B[k // 16, np.arange(N)[None, :]] >> (2 * (k % 16)).astype(np.uint32)) & 3
     want = np.array([0, 1, -2, -1], np.float32)[codes]
-    for k0 in range(0, K, 4):
+    for k0 in range(0, 256, 4):
         eye = np.zeros((4, K))
         eye[np.arange(4), k0 + np.arange(4)] = 1.0
         c = dict(A=synth.to_dt(eye, 0), B=B, S=S, other=None, bias=None)
-        out = synth.from_dt(run(tl, c, 4, K, N, 0, 0, False, algo), 0)
+        out = synth.from_dt(run(tl, c, 4, K, N, 0, 0, False, algo, tl.Workspace()), 0)
         assert np.array_equal(out, want[k0:k0 + 4]), k0
 
 
+@pytest.mark.parametrize("impl", ["digit", "stream"])
 @pytest.mark.parametrize("bf16", [0, 1])
-def test_digit_outliers_and_zero_rows(cuda, tl, gemv_algo, bf16):
+def test_digit_outliers_and_zero_rows(cuda, tl, gemv_algo, bf16, impl):
     # rows with a large outlier (the fixed-point step follows the row maximum), a row of
     # tiny values and an all-zero row
     from ternocl_b200 import synth
-    algo = gemv_algo("digit")
+    algo = gemv_algo(impl)
     M, K, N = 4, 4096, 1024
     c = int2_case(77, M, K, N, bf16)
     A = synth.from_dt(c["A"], bf16).astype(np.float64)
@@ -164,12 +168,13 @@ def test_digit_outliers_and_zero_rows(cuda, tl, gemv_algo, bf16):
     check_output(out, int2_gold_out(c, M, K, N, bf16, 0, True), bf16, True, "digit outliers fp32")
 
 
-def test_digit_row_max_positions(cuda, tl, gemv_algo):
+@pytest.mark.parametrize("impl", ["digit", "stream"])
+def test_digit_row_max_positions(cuda, tl, gemv_algo, impl):
     # the fixed-point exponent follows each row's largest |A|: put it in every position of
     # a 16-byte load (low and high halves of each 32-bit pair) with larger values elsewhere
     # in the other half-words, so a lost maximum would overflow the digits
     from ternocl_b200 import synth
-    algo = gemv_algo("digit")
+    algo = gemv_algo(impl)
     M, K, N = 4, 1024, 256
     c = int2_case(91, M, K, N, 0)
     for pos in range(8):
@@ -180,4 +185,4 @@ def test_digit_row_max_positions(cuda, tl, gemv_algo):
         A[1] *= -1.0
         c["A"] = synth.to_dt(A, 0)
         gold = int2_gold_out(c, M, K, N, 0, 0, False)
-        check_output(run(tl, c, M, K, N, 0, 0, False, algo), gold, 0, False, "max at %d" % pos)
+        check_output(run(tl, c, M, K, N, 0, 0, False, algo, tl.Workspace()), gold, 0, False, "max at %d" % pos)

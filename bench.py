@@ -1024,15 +1024,22 @@ def main():
     # A decode loop replays captured launches: on one GPU the K timed steps (4 GEMV
     # launches each, weight set i % nsets) are captured once into a CUDA graph and the
     # timed region is one replay of it (the C ABI allocates nothing, so its calls capture).
+    # With N GPUs the fused column-sharded GEMV keeps its handshake epoch on the device, so
+    # its steps are captured the same way on every rank and the ranks replay together.
     timed_graph = None
-    if world == 1 and args.graph:
+    if args.graph and (world == 1 or fused is not None):
         torch.cuda.synchronize()
         timed_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(timed_graph):
             cs = torch.cuda.current_stream(dev).cuda_stream
             for i in range(args.steps):
-                for ly in layers:
-                    gemv(ly, i % nsets, cs)
+                for j, ly in enumerate(layers):
+                    if fused is not None:
+                        fused[j](ly["A"], ly["B"][i % nsets], ly["S"][i % nsets], stream=cs)
+                    else:
+                        gemv(ly, i % nsets, cs)
+        if world > 1:
+            dist.barrier(device_ids=[local])
         timed_graph.replay()  # the first replay uploads the graph: keep it out of the timed region
         torch.cuda.synchronize()
 
@@ -1144,9 +1151,9 @@ def main():
     if world == 1 and not args.no_secondary:
         tf, pms, _ = prefill_measure(tl, synth, dev, steps=min(args.steps, 20), warmup=3)
         pk = peaks_tensor(pms * min(args.steps, 20) * 1e-3)
-        pk_moe = peaks_tensor(mms * min(args.steps, 10) * 1e-3)
         mt, mtf, mms, me2e, mcpu = moe_measure(tl, synth, dev, steps=min(args.steps, 10), warmup=2,
                                                cpu=not args.no_cpu_baseline)
+        pk_moe = peaks_tensor(mms * min(args.steps, 10) * 1e-3)
         secondary_moe = {"metric": "MoE prefill tokens/s (T=4096, H=2048, I=768, E=128, top-8, fp16)", "value": mt,
                          "unit": "tokens/s", "ms_per_layer": mms, "tflops": mtf,
                          "roofline": {"bound": "tensor", "achieved": mtf, "peak": pk_moe[0], "unit": "TFLOP/s",
@@ -1174,7 +1181,7 @@ def main():
                                        "all-gather fused into the GEMV epilogue (NVLink peer stores)"))
                        if world > 1 else "single GPU",
                        "pdl": not args.no_pdl,
-                       "launch": "one CUDA graph of the K timed steps" if (args.graph and world == 1) else "host calls, PDL"},
+                       "launch": "one CUDA graph of the K timed steps" if timed_graph is not None else "host calls, PDL"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "kernel": "gemv_i2d_kernel (integer-MMA int2 GEMV)", "launches": launches,

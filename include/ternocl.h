@@ -98,7 +98,8 @@ int ternocl_device_error(int reset);
  *    (M <= 4; the default there when no workspace is given), 3 = the same arithmetic in a
  *    persistent kernel fed by TMA with a stream-K split (M = 1; opt-in), 4 = the same
  *    arithmetic in one balanced wave of one CTA per SM, each warp streaming a contiguous
- *    range of (strip, 128-row group) units (M <= 4 with a workspace; the default there).
+ *    range of (strip, 128-row group) units (M <= 4 with a workspace; opt-in: measured
+ *    about 2x slower than 2 on the Llama-3-8B shapes).
  *  TERNOCL_OPT_GEMV_STAGES (default 0 = planned): units (1 KB of weights each) in flight
  *    per warp in the stream-K GEMV of GEMV_IMPL 4: 4, 6 or 8.
  *  TERNOCL_OPT_PEER_TIMEOUT_MS (default 2000, 1..60000): how long the column-sharded GEMV

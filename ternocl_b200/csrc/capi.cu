@@ -247,9 +247,9 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
         return cuda_status(int2_gemv_p_launch(a));
     }
     const bool digit = M <= kGemvDigitMaxM && impl != 1;
-    if (digit && !peer && ws && (impl == 0 || impl == 4)) {
-        // stream-K integer-MMA GEMV: one balanced wave; small enough (<= ~110 KB of shared
-        // memory) that the next GEMV of the stream fits beside it on every SM
+    if (digit && ws && impl == 4) {
+        // stream-K integer-MMA GEMV (opt-in): one balanced wave; small enough (<= ~110 KB
+        // of shared memory) that the next GEMV of the stream fits beside it on every SM
         const int ctas = int2_gemv_s_ctas(M, N, K, sm_count());
         int depth = options().gemv_stages;
         if (!depth) {

@@ -61,6 +61,16 @@ struct I2SParams {
     int M, N, K;
     float *part;    // [PW][2][M][32] fp32 partials of split strips
     unsigned *cnt;  // [strips] arrival counters (zero between calls)
+    // column-sharded mode (world > 0): these are columns [n_off, n_off + N) of an output of
+    // N_out columns; each finished strip is stored into every rank's C_peer[r] (Other and
+    // Bias are full width), then gemv::peer_complete runs the ranks' flag handshake
+    int world, rank, n_off, N_out;
+    unsigned epoch;
+    unsigned long long peer_timeout_ns;
+    unsigned *done_cnt;
+    unsigned *err;
+    void *C_peer[gemv::kMaxPeers];
+    unsigned *flag_peer[gemv::kMaxPeers];
 };
 
 __host__ __device__ constexpr int nmma_for(int rows) { return (4 * rows + 7) / 8; }
@@ -76,10 +86,17 @@ __host__ __device__ inline size_t i2s_smem(int W, int D, int rows, int K) {
            + (size_t)rows * (K / kGS) * 8;                    // per (row, group): exponent, 2^-e / 64
 }
 
-// warp holding unit u (u0(w) = floor(U w / PW) <= u < u0(w+1))
-__device__ __forceinline__ int warp_of(long long u, long long U, int PW) {
-    return (int)(((u + 1) * PW - 1) / U);
-}
+// Balanced split of U units over PW warps in 32-bit arithmetic (U < 2^31, PW <= U):
+// warp w holds q + (w < r) units starting at w q + min(w, r), U = q PW + r.
+struct UnitSplit {
+    int q, r;
+    __device__ __forceinline__ UnitSplit(int U, int PW) : q(U / PW), r(U - (U / PW) * PW) {}
+    __device__ __forceinline__ int start(int w) const { return w * q + min(w, r); }
+    __device__ __forceinline__ int warp_of(int u) const {
+        const int b = r * (q + 1);
+        return u < b ? u / (q + 1) : r + (u - b) / q;
+    }
+};
 
 using digit::cls;
 using digit::imma;
@@ -94,10 +111,11 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
     const int gl = lane >> 2, t = lane & 3;
     const int G = p.K / kGS;
     const int strips = (p.N + kCols - 1) / kCols;
-    const long long U = (long long)strips * G;
+    const int U = strips * G;
     const int PW = gridDim.x * W;
     const int wid = blockIdx.x * W + warp;
-    const long long u0 = U * wid / PW, u1 = U * (wid + 1) / PW;
+    const UnitSplit split(U, PW);
+    const int u0 = split.start(wid), u1 = split.start(wid + 1);
     const int rows = p.M;
     const int pstride = plane_stride(p.K);
 
@@ -110,8 +128,8 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
     float *gfac = reinterpret_cast<float *>(gexp + rows * G);
 
     // ---- weight stream: unit u -> stage (u - u0) mod D -------------------------------
-    long long ld_u = u0;
-    int ld_s = (int)(u0 / G), ld_g = (int)(u0 - (long long)ld_s * G), ld_stage = 0;
+    int ld_u = u0;
+    int ld_s = u0 / G, ld_g = u0 - ld_s * G, ld_stage = 0;
     auto issue = [&]() {
         if (ld_u < u1) {
             char *st = ring + ld_stage * kStageBytes;
@@ -133,6 +151,15 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
     };
 #pragma unroll
     for (int i = 0; i < D - 1; ++i) issue();
+    // the rest of this warp's units into L2: per unit its 8 word rows and its scale row
+    for (int ub = u0 + D - 1; ub < u1; ub += 4) {
+        const int u = ub + (lane >> 3);
+        if (u < u1) {
+            const int s = u / G, g = u - s * G, col = s * kCols;
+            gemv::prefetch_l2(p.B + (size_t)(g * 8 + (lane & 7)) * p.N + col);
+            if ((lane & 7) == 0) gemv::prefetch_l2(p.S + (size_t)g * p.N + col);
+        }
+    }
     // The weights never depend on the previous kernel: their first D - 1 units are in
     // flight already.  Let the next kernel of the stream be scheduled (its own
     // griddepcontrol.wait still covers this whole grid), then wait for ours.
@@ -204,7 +231,7 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
             for (int c = 0; c < 4; ++c) acc[b][tt][c] = 0.0f;
 
     // ---- finish a strip: planes -> values, then store or hand over as a partial -------
-    const int first_strip = (int)(u0 / G);
+    const int first_strip = u0 / G;
     auto flush = [&](int cs, bool whole) {
         __syncwarp();
 #pragma unroll
@@ -236,8 +263,8 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
                 if (m < rows) __stcg(mine + m * kCols, v[m]);
             __threadfence();
             __syncwarp();
-            const long long su = (long long)cs * G;
-            const int wf = warp_of(su, U, PW), wl = warp_of(su + G - 1, U, PW);
+            const int su = cs * G;
+            const int wf = split.warp_of(su), wl = split.warp_of(su + G - 1);
             unsigned last = 0;
             if (lane == 0) last = atomicAdd(p.cnt + cs, 1u) == (unsigned)(wl - wf) ? 1u : 0u;
             last = __shfl_sync(0xffffffffu, last, 0);
@@ -246,8 +273,7 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
 #pragma unroll
             for (int m = 0; m < kMaxRows; ++m) v[m] = 0.0f;
             for (int w2 = wf; w2 <= wl; ++w2) {
-                const long long w2u0 = U * w2 / PW;
-                const int slot2 = (w2u0 / G == cs) ? 0 : 1;
+                const int slot2 = split.start(w2) >= su ? 0 : 1;  // strip cs is w2's first or last
                 const float *pp = p.part + ((size_t)(w2 * 2 + slot2) * rows) * kCols + lane;
 #pragma unroll
                 for (int m = 0; m < kMaxRows; ++m)
@@ -256,15 +282,24 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
             if (lane == 0) p.cnt[cs] = 0u;  // ready for the next call
         }
         if (colok) {
+            if (p.world > 0) {  // column-sharded: this rank's columns into every rank's C
+                for (int r = 0; r < p.world; ++r)
 #pragma unroll
-            for (int m = 0; m < kMaxRows; ++m)
-                if (m < rows) epi_store<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, col, v[m]);
+                    for (int m = 0; m < kMaxRows; ++m)
+                        if (m < rows)
+                            epi_store<DT, POSTOP, OUT_F32>(p.C_peer[r], p.Other, p.Bias, p.N_out, m, p.n_off + col,
+                                                           v[m]);
+            } else {
+#pragma unroll
+                for (int m = 0; m < kMaxRows; ++m)
+                    if (m < rows) epi_store<DT, POSTOP, OUT_F32>(p.C, p.Other, p.Bias, p.N, m, col, v[m]);
+            }
         }
     };
 
     // ---- main loop over this warp's units ---------------------------------------------
-    int cs = first_strip, cg = (int)(u0 - (long long)first_strip * G), seg_g0 = cg, stage = 0;
-    for (long long u = u0; u < u1; ++u) {
+    int cs = first_strip, cg = u0 - first_strip * G, seg_g0 = cg, stage = 0;
+    for (int u = u0; u < u1; ++u) {
         gemv::cp_async_wait<D - 2>();
         __syncwarp();  // the scale copies of lanes t == 0 are visible to the whole warp
         const char *st = ring + stage * kStageBytes;
@@ -333,6 +368,7 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
             ++cg;
         }
     }
+    if (p.world > 0) gemv::peer_complete(p, p.err);
 }
 
 template <int W, int D, int NMMA, class DT, int POSTOP, bool OUT_F32>
@@ -349,6 +385,18 @@ cudaError_t launch_i2s(const GemvArgs &a, int ctas) {
     p.K = a.K;
     p.cnt = a.ws_cnt;
     p.part = a.ws_part;
+    p.world = a.world;
+    p.rank = a.rank;
+    p.n_off = a.n_off;
+    p.N_out = a.N_out;
+    p.epoch = a.epoch;
+    p.peer_timeout_ns = (unsigned long long)options().peer_timeout_ms * 1000000ull;
+    p.done_cnt = a.done_cnt;
+    p.err = a.err;
+    for (int r = 0; r < gemv::kMaxPeers; ++r) {
+        p.C_peer[r] = r < a.world ? a.C_peer[r] : nullptr;
+        p.flag_peer[r] = r < a.world ? a.flag_peer[r] : nullptr;
+    }
     const size_t smem = i2s_smem(W, D, a.M, a.K);
     auto kern = gemv_i2s_kernel<W, D, NMMA, DT, POSTOP, OUT_F32>;
     cudaError_t e = ensure_smem(kern, smem);
@@ -376,6 +424,7 @@ size_t int2_gemv_s_smem(int M, int K, int depth) { return i2s_smem(kI2SWarps, de
 int int2_gemv_s_ctas(int M, int N, int K, int sms) {
     if (M < 1 || M > kMaxRows) return 0;
     const long long U = (long long)((N + kCols - 1) / kCols) * (K / kGS);
+    if (U >= (1ll << 31)) return 0;  // the kernel splits units in 32-bit arithmetic
     long long ctas = U / kI2SWarps;  // every warp gets at least one unit
     if (ctas > sms) ctas = sms;
     return (int)ctas;

@@ -733,10 +733,15 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
     gen = torch.Generator(device=dev)
     gen.manual_seed(41)
     rng = np.random.default_rng(41)
-    host_bufs, bufs, S = {}, {}, {}
+    host_bufs, bufs, srs, S = {}, {}, {}, {}
+    LS = 4
+    while LS > 1 and K % (64 * LS):
+        LS //= 2
     for zi, z in enumerate(BITCOS["z"]):
         host_bufs[z] = [tl.bitcos_random(K, N, z, 100 * zi + k) for k in range(BITCOS["sets"])]
         bufs[z] = [torch.from_numpy(b.view(np.int32)).to(dev) for b in host_bufs[z]]
+        # slice ranks at the reference driver's default LS = 4 (bitcos_fp16_upcvt/main.cpp:122-123,194)
+        srs[z] = [torch.from_numpy(tl.bitcos_slice_ranks(b, K, N, LS).view(np.int32)).to(dev) for b in host_bufs[z]]
         S[z] = (torch.rand(K // 128, N, generator=gen, device=dev) * 0.04 + 0.01).half()
     signs_h = np.where(rng.random(K) < 0.5, -1, 1).astype(np.int8)
     signs = torch.from_numpy(signs_h).to(dev)
@@ -752,8 +757,8 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
 
     def gemv(M, z, i):
         check(tl, "ternocl_bitcos_upcvt", L.ternocl_bitcos_upcvt(Y[M].data_ptr(), bufs[z][i].data_ptr(),
-                                                                 S[z].data_ptr(), None, 1, C[M].data_ptr(), None,
-                                                                 None, M, N, K, 0, 0, 0, 0, sp))
+                                                                 S[z].data_ptr(), srs[z][i].data_ptr(), LS,
+                                                                 C[M].data_ptr(), None, None, M, N, K, 0, 0, 0, 0, sp))
 
     per = []
     for M in BITCOS["M"]:
@@ -785,7 +790,7 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
     peak, peak_kind = peaks()
     out = {"metric": BITCOS_METRIC, "value": value, "unit": "GB/s", "ms_per_step": sum(q["us_per_call"] for q in m1) / 1e3,
            "dtype": "fp16",
-           "config": {"workload": "bitcos_fp16_upcvt + hadamard_fwht (configs[3])", "K": K, "N": N, "HB": HB,
+           "config": {"workload": "bitcos_fp16_upcvt + hadamard_fwht (configs[3])", "K": K, "N": N, "HB": HB, "LS": LS,
                       "z": list(BITCOS["z"]), "M": list(BITCOS["M"]),
                       "l2": "inputs larger than L2: %d BITCOS buffers (~%d MB) rotated per call" % (
                           len(BITCOS["z"]) * BITCOS["sets"], sum(b.size * 4 for z in BITCOS["z"] for b in host_bufs[z]) >> 20),

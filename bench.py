@@ -919,6 +919,8 @@ def main():
                          "(quant_a + GEMM); bitcos: configs[3], Hadamard + BITCOS GEMV/GEMM; moe: the MoE prefill "
                          "layer (expert-parallel on N GPUs); hadamard: the sign flip + FWHT of the BITCOS config")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--shard-all", action="store_true",
+                    help="N>1: split every layer's columns over the ranks (default: only where it pays)")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="N>1: GEMV + NCCL all-gather instead of the GEMV with the all-gather fused in its epilogue")
     ap.add_argument("--graph", dest="graph", action="store_true", default=True,
@@ -957,20 +959,34 @@ def main():
     if args.workload in ("int8", "bitcos"):
         return run_replicated(args, tl, dev, world, rank, local)
 
+    # With N GPUs: splitting a layer's columns over the ranks (the all-gather fused into
+    # the GEMV) pays only where it saves more weight-streaming time per rank than the
+    # sharded launch's completion costs (dist.shard_pays, measured ~10 us at two ranks),
+    # which none of these layers does.  So by default the N ranks run N independent
+    # decode streams (replicas: each rank the whole step on its own weights, no
+    # collective; weak scaling, the value counts every rank's weights).  --shard-all (the
+    # fused all-gather) or --nccl-gather split every layer instead (strong scaling, each
+    # layer's weights counted once).
+    from ternocl_b200 import dist as tdist
+    sharded = world > 1 and (args.shard_all or args.nccl_gather)
+    shard = {(K, N): sharded for K, N in SHAPES}
+
     # per-rank column slices (multiples of 16)
-    def cols(N):
+    def cols(K, N):
+        if not shard[(K, N)]:
+            return 0, N
         per = (N // world) // 16 * 16
         n0 = rank * per
         return n0, (per if rank < world - 1 else N - n0)
 
-    set_bytes = sum(weight_bytes(K, cols(N)[1]) for K, N in SHAPES)
+    set_bytes = sum(weight_bytes(K, cols(K, N)[1]) for K, N in SHAPES)
     full_set_bytes = sum(weight_bytes(K, N) for K, N in SHAPES)
     nsets = args.sets or max(1, int(np.ceil(WEIGHTS_GIB * (1 << 30) / full_set_bytes)))
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     layers = []  # per shape: dict
     for K, N in SHAPES:
-        n0, nl = cols(N)
+        n0, nl = cols(K, N)
         rng = np.random.default_rng(K * 7 + N)
         A = torch.randn(M, K, generator=g, device=dev).half()
         # one packed set generated on the host (uniform ternary), further sets are
@@ -982,9 +998,9 @@ def main():
             Bs.append(B0.view(-1)[perm].view_as(B0).contiguous())
             Ss.append((torch.rand(K // 128, nl, generator=g, device=dev) * 0.04 + 0.01).half())
         C = torch.empty(M, nl, dtype=torch.float16, device=dev)
-        Cfull = torch.empty(world, M, nl, dtype=torch.float16, device=dev) if world > 1 else None
+        Cfull = torch.empty(world, M, nl, dtype=torch.float16, device=dev) if shard[(K, N)] else None
         ws = tl.Workspace(dev, tl.gemv_workspace_size(M, nl, K))
-        layers.append(dict(K=K, N=N, n0=n0, nl=nl, A=A, B=Bs, S=Ss, C=C, Cfull=Cfull, ws=ws))
+        layers.append(dict(K=K, N=N, n0=n0, nl=nl, A=A, B=Bs, S=Ss, C=C, Cfull=Cfull, ws=ws, shard=shard[(K, N)]))
     del B0
     torch.cuda.synchronize()
 
@@ -1001,19 +1017,22 @@ def main():
 
     fused = None
     if world > 1 and not args.nccl_gather:
-        from ternocl_b200 import dist as tdist
-        fused = [tdist.FusedAllGatherGemv(M, ly["N"], ly["K"], torch.float16, dev) for ly in layers]
+        fused = [tdist.FusedAllGatherGemv(M, ly["N"], ly["K"], torch.float16, dev) if ly["shard"] else None
+                 for ly in layers]
 
     def step(i):
         s = i % nsets
         if fused is not None:  # each launch leaves the full C on every rank
             for ly, fg in zip(layers, fused):
-                fg(ly["A"], ly["B"][s], ly["S"][s])
+                if fg is not None:
+                    fg(ly["A"], ly["B"][s], ly["S"][s])
+                else:
+                    gemv(ly, s)
             return
         for ly in layers:
             gemv(ly, s)
-        if world > 1:
-            for ly in layers:
+        for ly in layers:
+            if ly["shard"]:
                 dist.all_gather_into_tensor(ly["Cfull"], ly["C"])
 
     def barrier():
@@ -1039,7 +1058,7 @@ def main():
             cs = torch.cuda.current_stream(dev).cuda_stream
             for i in range(args.steps):
                 for j, ly in enumerate(layers):
-                    if fused is not None:
+                    if fused is not None and fused[j] is not None:
                         fused[j](ly["A"], ly["B"][i % nsets], ly["S"][i % nsets], stream=cs)
                     else:
                         gemv(ly, i % nsets, cs)
@@ -1073,7 +1092,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    value = full_set_bytes / (ms_per_step * 1e-3) / 1e9  # all ranks' weights per step
+    # the whole job's weights per step: each layer once when sharded, every rank's own
+    # copy when the ranks are independent replicas
+    job_bytes = full_set_bytes * (world if (world > 1 and not sharded) else 1)
+    value = job_bytes / (ms_per_step * 1e-3) / 1e9
 
     # kernel-only timing (no collectives) for the roofline: GEMV launches back to back
     ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1099,7 +1121,7 @@ def main():
     hC = [torch.empty(M, ly["nl"], dtype=torch.float16).pin_memory() for ly in layers]
     h2d = sum(x.numel() * 2 for x in hA)
     d2h = sum(x.numel() * 2 for x in hC)
-    packed = fused is None and world == 1
+    packed = not sharded  # one GPU, or independent replicas: each rank the whole step
     if packed:
         ka = [ly["K"] * M for ly in layers]
         kc = [ly["nl"] * M for ly in layers]
@@ -1123,12 +1145,12 @@ def main():
             return
         for j, ly in enumerate(layers):
             ly["A"].copy_(hA[j], non_blocking=True)
-            if fused is not None:
+            if fused is not None and fused[j] is not None:
                 out = fused[j](ly["A"], ly["B"][s], ly["S"][s])
                 hC[j].copy_(out[:, ly["n0"]:ly["n0"] + ly["nl"]], non_blocking=True)
                 continue
             gemv(ly, s)
-            if world > 1:
+            if ly["shard"]:
                 dist.all_gather_into_tensor(ly["Cfull"], ly["C"])
             hC[j].copy_(ly["C"], non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
@@ -1145,7 +1167,7 @@ def main():
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = full_set_bytes / e2e_s / 1e9
+    e2e_value = job_bytes / e2e_s / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1177,13 +1199,16 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "higher_is_better": True, "scaling": "weak" if (world > 1 and not sharded) else "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "M": M, "shapes_KxN": SHAPES, "weight_sets": nsets,
                        "weights_gib": round(nsets * full_set_bytes / 2 ** 30, 3),
                        "l2": "inputs larger than L2: %d rotating weight sets" % nsets,
-                       "parallelism": ("N-sharded columns x%d + %s" % (world, "NCCL all-gather" if args.nccl_gather else
-                                       "all-gather fused into the GEMV epilogue (NVLink peer stores)"))
+                       "parallelism": ("N-sharded columns x%d + %s" % (
+                           world, "NCCL all-gather" if args.nccl_gather else
+                           "all-gather fused into the GEMV epilogue (NVLink peer stores)")) if sharded else
+                       ("%d independent decode streams (replicas, no collective): column sharding saves less "
+                        "than a sharded launch's completion (~10 us at 2 ranks) on every layer" % world)
                        if world > 1 else "single GPU",
                        "pdl": not args.no_pdl,
                        "launch": "one CUDA graph of the K timed steps" if timed_graph is not None else "host calls, PDL"},
@@ -1205,7 +1230,8 @@ def main():
     if fused is not None:
         torch.cuda.synchronize()
         for fg in fused:
-            fg.close()
+            if fg is not None:
+                fg.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -165,10 +165,12 @@ int ternocl_int2_upcvt_noalloc(const void *A, const uint32_t *B, const void *S, 
  * the reference, which runs on one device; it replaces a GEMV per rank followed by an
  * NCCL all-gather of the outputs).  Rank `rank` of `world` (<= 8) holds the columns
  * [n0, n0 + nl) of the weights (B [K/16, nl], S [K/128, nl], contiguous shards) and
- * stores C[:, n0:n0+nl] into every rank's full C_ranks[r] ([M, N], device pointers valid
- * in this process, e.g. CUDA IPC mappings of the peers' buffers; Other [M, N] and Bias
- * [N] are full width).  The launch completes only after all ranks' columns have
- * arrived: the grid's last CTA writes `epoch` into flags_ranks[r][rank] of every rank and
+ * stores C[:, n0:n0+nl] into every rank's full C_ranks[r] ([M, N], 16-byte aligned device
+ * pointers valid in this process, e.g. CUDA IPC mappings of the peers' buffers; Other
+ * [M, N] and Bias [N] are full width): the CTAs store into this rank's own C, and the
+ * grid's last CTA copies the slice into the other ranks' C over peer stores.  The launch
+ * completes only after all ranks' columns have arrived: that CTA then writes `epoch`
+ * into flags_ranks[r][rank] of every rank and
  * waits until flags_ranks[rank][r] >= epoch for all r (bounded; a timeout sets bit 2 of
  * ternocl_device_error).  flags start at 0 and a nonzero `epoch` must increase by one per
  * call, in the same order on every rank.  A rank must not read a C buffer after it has

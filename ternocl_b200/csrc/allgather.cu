@@ -106,7 +106,7 @@ int ternocl_int2_upcvt_allgather(const void *A, const uint32_t *B, const void *S
         n0 + nl > N)
         return TERNOCL_ERR_SHAPE;
     for (int r = 0; r < world; ++r)
-        if (!C_ranks[r] || !flags_ranks[r] || ((uintptr_t)C_ranks[r] % (out_f32 ? 16 : 8))) return TERNOCL_ERR_ARG;
+        if (!C_ranks[r] || !flags_ranks[r] || ((uintptr_t)C_ranks[r] % 16)) return TERNOCL_ERR_ARG;  // 16-byte slice copy
     if (!ws || ((uintptr_t)ws % 256) || ws_bytes < ternocl_gemv_allgather_workspace_size(M, nl, K))
         return TERNOCL_ERR_WORKSPACE;
     if (M == 0) return TERNOCL_OK;

@@ -63,7 +63,8 @@ struct Params {
     const uint16_t *SA;
     int ldsa, qmode;
     // column-sharded mode (world > 0): this grid computes columns [n_off, n_off + N) of a
-    // C with N_out columns and stores them into every rank's copy C_peer[r]; Other and
+    // C with N_out columns and stores them into its own rank's copy C_peer[rank], which
+    // peer_complete then copies into every other rank's copy C_peer[r]; Other and
     // Bias are the full-width arrays.  flag_peer[r] = rank r's flags (one per rank).
     int world, rank, n_off, N_out;
     unsigned epoch;               // 0: kept on the device in flag_peer[rank][world]
@@ -231,17 +232,16 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
     for (int i = 0; i < 4; ++i) cols[i] = n0 + ColMap::thread_col(g, i);
 
     auto store = [&]() {
-        if (p.world > 0) {  // column-sharded: this rank's columns into every rank's C
+        if (p.world > 0) {  // column-sharded: this rank's columns into its own copy of C
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int m = mb + 2 * q + h;
                 if (m < p.M) {
-                    for (int r = 0; r < p.world; ++r) {
-                        epi_store2<DT, POSTOP, OUT_F32>(p.C_peer[r], p.Other, p.Bias, p.N_out, m, p.n_off + cols[0],
-                                                        v[4 * h], v[4 * h + 1]);
-                        epi_store2<DT, POSTOP, OUT_F32>(p.C_peer[r], p.Other, p.Bias, p.N_out, m, p.n_off + cols[2],
-                                                        v[4 * h + 2], v[4 * h + 3]);
-                    }
+                    void *Cl = p.C_peer[p.rank];
+                    epi_store2<DT, POSTOP, OUT_F32>(Cl, p.Other, p.Bias, p.N_out, m, p.n_off + cols[0], v[4 * h],
+                                                    v[4 * h + 1]);
+                    epi_store2<DT, POSTOP, OUT_F32>(Cl, p.Other, p.Bias, p.N_out, m, p.n_off + cols[2], v[4 * h + 2],
+                                                    v[4 * h + 3]);
                 }
             }
             return;
@@ -325,12 +325,15 @@ __device__ __forceinline__ void finish(const Params &p, char *smem, float v[8], 
     if (lane == 0) p.ws_cnt[tile] = 0u;  // ready for the next call
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned *ptr, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
+// acquire-release fences (lighter than the sequentially consistent __threadfence*)
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;\n" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_sys(unsigned *ptr, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *ptr) {
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned *ptr) {
     unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
     return v;
 }
 __device__ __forceinline__ uint64_t gtimer_ns() {
@@ -339,40 +342,66 @@ __device__ __forceinline__ uint64_t gtimer_ns() {
     return t;
 }
 
-// Column-sharded completion: every CTA counts itself once its peer stores are fenced;
-// the last CTA of the grid writes the call's epoch into its slot of every rank's flags
-// and waits until every rank has written that epoch into this rank's flags, so the
-// launch completes only when the whole of C has arrived.  With p.epoch == 0 the epoch is
-// the rank's own call count, kept in flag_peer[rank][world] and bumped here (the same
-// sequence on every rank, and no host value in the launch: a graph replays it).  The
-// wait gives up after p.peer_timeout_ns (error word bit 2) and the kernel returns.
+// Column-sharded completion.  Every CTA has stored its columns into this rank's own copy
+// of C; after a CTA barrier one thread makes them visible on the GPU (fence) and counts
+// the CTA in.  The last CTA of the grid copies the rank's whole column slice (M rows x N
+// columns, esz bytes each, in 16-byte pieces) into every other rank's copy over peer
+// stores; after a CTA barrier one thread makes those stores visible to the system (one
+// acquire-release fence at system scope, cumulative over the CTA's stores, as a grid
+// barrier does at GPU scope), writes the call's epoch into its slot of every rank's flags (relaxed system-
+// scope stores), polls until every rank has written that epoch into this rank's flags
+// (relaxed system-scope loads) and then fences again (acquire), so the launch completes
+// only when the whole of C has arrived.  With p.epoch == 0 the epoch is the rank's own
+// call count, kept in flag_peer[rank][world] and bumped here (the same sequence on every
+// rank, and no host value in the launch: a graph replays it).  The wait gives up after
+// p.peer_timeout_ns (error word bit 2) and the kernel returns.
 template <class P>
-__device__ __forceinline__ void peer_complete(const P &p, unsigned *err) {
+__device__ __forceinline__ void peer_complete(const P &p, unsigned *err, int esz) {
+    __shared__ unsigned s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        fence_acq_rel_gpu();  // release: the CTA's stores of this rank's slice
+        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        s_last = atomicAdd(p.done_cnt, 1u) == total - 1 ? 1u : 0u;
+        if (s_last) fence_acq_rel_gpu();  // acquire: every CTA's stores
+    }
+    __syncthreads();
+    if (!s_last) return;
+    const size_t row_bytes = (size_t)p.N * esz, pitch = (size_t)p.N_out * esz, off = (size_t)p.n_off * esz;
+    const int pieces = (int)(row_bytes / 16), total_pieces = pieces * p.M;
+    const char *src = reinterpret_cast<const char *>(p.C_peer[p.rank]);
+    for (int r = 0; r < p.world; ++r) {
+        if (r == p.rank) continue;
+        char *dst = reinterpret_cast<char *>(p.C_peer[r]);
+        for (int i = threadIdx.x; i < total_pieces; i += blockDim.x) {
+            const int m = i / pieces, c = i - m * pieces;
+            const size_t o = (size_t)m * pitch + off + (size_t)c * 16;
+            *reinterpret_cast<uint4 *>(dst + o) = __ldcg(reinterpret_cast<const uint4 *>(src + o));
+        }
+    }
     __syncthreads();
     if (threadIdx.x != 0) return;
-    __threadfence_system();
-    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
-    if (atomicAdd(p.done_cnt, 1u) != total - 1) return;
-    *p.done_cnt = 0u;  // ready for the next launch
-    __threadfence_system();
+    fence_acq_rel_sys();  // release: the CTA's peer stores, visible to the system before the flags
+    *p.done_cnt = 0u;        // ready for the next launch
     unsigned epoch = p.epoch;
     if (epoch == 0u) {
         unsigned *count = p.flag_peer[p.rank] + p.world;
         epoch = *count + 1u;
         *count = epoch;
     }
-    for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_peer[r] + p.rank, epoch);
+    for (int r = 0; r < p.world; ++r) st_relaxed_sys(p.flag_peer[r] + p.rank, epoch);
     const unsigned *mine = p.flag_peer[p.rank];
     const uint64_t t0 = gtimer_ns();
     for (int r = 0; r < p.world; ++r) {
         uint32_t i = 0;
-        while ((int)(ld_acquire_sys(mine + r) - epoch) < 0) {
+        while ((int)(ld_relaxed_sys(mine + r) - epoch) < 0) {
             if ((++i & 255u) == 0 && gtimer_ns() - t0 > p.peer_timeout_ns) {
                 atomicOr(err, 4u);
                 return;
             }
         }
     }
+    fence_acq_rel_sys();  // acquire: the peers' slices before the launch completes
 }
 
 template <class Policy, int W, class DT, int POSTOP, bool OUT_F32>
@@ -458,7 +487,7 @@ __global__ void __launch_bounds__(W * 32) gemv_kernel(const Params p) {
     Policy::thread_values(acc, v);  // v[h*4 + i]: activation row mb+2q+h, column col(i)
     __syncthreads();  // the ring is reused for the reduction
     finish<Policy, W, DT, POSTOP, OUT_F32>(p, smem, v, colok);
-    if (p.world > 0) peer_complete(p, p.err);
+    if (p.world > 0) peer_complete(p, p.err, OUT_F32 ? 4 : 2);
 }
 
 }  // namespace gemv

@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(W * 32) gemv_i2d_kernel(const gemv::Params p) 
     }
     __syncthreads();  // the rings are reused for the reduction
     gemv::finish<I2DCols, W, DT, POSTOP, OUT_F32>(p, smem, v, n0 + 4 * g < p.N);
-    if (p.world > 0) gemv::peer_complete(p, p.err);
+    if (p.world > 0) gemv::peer_complete(p, p.err, OUT_F32 ? 4 : 2);
 }
 
 template <int W, int NMMA, class DT, int POSTOP, bool OUT_F32>

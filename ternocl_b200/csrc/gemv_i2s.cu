@@ -62,8 +62,9 @@ struct I2SParams {
     float *part;    // [PW][2][M][32] fp32 partials of split strips
     unsigned *cnt;  // [strips] arrival counters (zero between calls)
     // column-sharded mode (world > 0): these are columns [n_off, n_off + N) of an output of
-    // N_out columns; each finished strip is stored into every rank's C_peer[r] (Other and
-    // Bias are full width), then gemv::peer_complete runs the ranks' flag handshake
+    // N_out columns; each finished strip is stored into this rank's C_peer[rank] (Other and
+    // Bias are full width), then gemv::peer_complete copies the slice to the other ranks
+    // and runs their flag handshake
     int world, rank, n_off, N_out;
     unsigned epoch;
     unsigned long long peer_timeout_ns;
@@ -282,13 +283,12 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
             if (lane == 0) p.cnt[cs] = 0u;  // ready for the next call
         }
         if (colok) {
-            if (p.world > 0) {  // column-sharded: this rank's columns into every rank's C
-                for (int r = 0; r < p.world; ++r)
+            if (p.world > 0) {  // column-sharded: this rank's columns into its own copy of C
 #pragma unroll
-                    for (int m = 0; m < kMaxRows; ++m)
-                        if (m < rows)
-                            epi_store<DT, POSTOP, OUT_F32>(p.C_peer[r], p.Other, p.Bias, p.N_out, m, p.n_off + col,
-                                                           v[m]);
+                for (int m = 0; m < kMaxRows; ++m)
+                    if (m < rows)
+                        epi_store<DT, POSTOP, OUT_F32>(p.C_peer[p.rank], p.Other, p.Bias, p.N_out, m, p.n_off + col,
+                                                       v[m]);
             } else {
 #pragma unroll
                 for (int m = 0; m < kMaxRows; ++m)
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(W * 32, 2) gemv_i2s_kernel(const I2SParams p) 
             ++cg;
         }
     }
-    if (p.world > 0) gemv::peer_complete(p, p.err);
+    if (p.world > 0) gemv::peer_complete(p, p.err, OUT_F32 ? 4 : 2);
 }
 
 template <int W, int D, int NMMA, class DT, int POSTOP, bool OUT_F32>

@@ -26,6 +26,26 @@ def column_shard(N, world, rank, align=16):
     return n0, (per if rank < world - 1 else N - n0)
 
 
+# Completion cost of one column-sharded GEMV launch (its last CTA copies the rank's slice
+# to the peers, fences at system scope and waits for the peers' flags), measured on B200:
+# ~4.5 us per call with one rank (no NVLink) and ~8-12 us with two; and the rate at
+# which a decode GEMV streams its weights (~2.5 TB/s on the Llama-3-8B shapes).
+SHARD_COMPLETION_US = 10.0
+SHARD_STREAM_GBS = 2500.0
+
+
+def shard_pays(K, N, world, completion_us=SHARD_COMPLETION_US, stream_gbs=SHARD_STREAM_GBS):
+    """Whether splitting the columns of a K x N int2 GEMV over `world` ranks saves more
+    weight-streaming time per rank than the sharded launch's completion costs.  Layers
+    for which it does not are better replicated (every rank runs the whole GEMV and has
+    the whole output, with no collective)."""
+    if world <= 1:
+        return False
+    weights = K * N // 4 + (K // 128) * N * 2
+    saved_us = weights * (1.0 - 1.0 / world) / (stream_gbs * 1e3)
+    return saved_us > completion_us
+
+
 def sharded_upcvt(A, B_shard, S_shard, N, upcvt=None, group=None, **kw):
     """C [M, N] = epi(A @ dequant(B, S)) with this rank holding columns column_shard(N, ...)."""
     if upcvt is None:

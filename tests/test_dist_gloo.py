@@ -63,3 +63,17 @@ def test_absent_rank_ends_the_collective_with_an_error(workers, tmp_path):
     d = torch.load(tmp_path / "absent_0.pt")
     assert d["outcome"].startswith("error"), d
     assert d["seconds"] < 30.0, d
+
+
+def test_shard_pays_policy():
+    # a layer is split over the ranks only where the weight-streaming time it saves per
+    # rank exceeds the sharded launch's completion cost; more ranks save more
+    from ternocl_b200 import dist as tdist
+    assert not tdist.shard_pays(4096, 28672, 1)
+    assert not tdist.shard_pays(4096, 28672, 2)  # 31 MB: ~6 us saved per rank, < 10 us
+    assert tdist.shard_pays(4096, 28672, 2, completion_us=5.0)
+    assert not tdist.shard_pays(4096, 4096, 8)  # 4.5 MB: under 2 us saved
+    assert tdist.shard_pays(5120, 248320, 2)  # a 27B lm_head (326 MB): ~65 us saved
+    for K, N in [(4096, 6144), (5120, 34816), (17408, 5120)]:
+        pays = [tdist.shard_pays(K, N, w) for w in (2, 4, 8)]
+        assert pays == sorted(pays)  # once it pays at some world size, it pays at larger ones

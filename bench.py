@@ -946,9 +946,17 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    import datetime
+    one_rank_group = False
     if world > 1:
-        import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    elif args.shard_all and args.workload == "decode":
+        # one GPU in the sharded mode: the fused all-gather GEMV with a single rank (its
+        # completion protocol without peers), for measuring that protocol's own cost
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev, timeout=datetime.timedelta(seconds=120))
+        one_rank_group = True
     tl.set_option(tl.OPT_PDL, 0 if args.no_pdl else 1)
     if args.workload == "prefill":
         return run_prefill(args, tl, synth, dev, world, rank, local)
@@ -968,7 +976,7 @@ def main():
     # fused all-gather) or --nccl-gather split every layer instead (strong scaling, each
     # layer's weights counted once).
     from ternocl_b200 import dist as tdist
-    sharded = world > 1 and (args.shard_all or args.nccl_gather)
+    sharded = (world > 1 and args.nccl_gather) or args.shard_all
     shard = {(K, N): sharded for K, N in SHAPES}
 
     # per-rank column slices (multiples of 16)
@@ -1016,7 +1024,7 @@ def main():
             raise tl.TernoclError("ternocl_int2_upcvt", st)
 
     fused = None
-    if world > 1 and not args.nccl_gather:
+    if (world > 1 and not args.nccl_gather) or one_rank_group:
         fused = [tdist.FusedAllGatherGemv(M, ly["N"], ly["K"], torch.float16, dev) if ly["shard"] else None
                  for ly in layers]
 
@@ -1232,7 +1240,7 @@ def main():
         for fg in fused:
             if fg is not None:
                 fg.close()
-    if world > 1:
+    if world > 1 or one_rank_group:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
 

@@ -838,6 +838,85 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
     return out
 
 
+# M=1 decode GEMV shapes of the reference's published table (int2_fp16_upcvt/README.md,
+# "Decode GEMV, M = 1"): name, K, N, the reference's published OpenCL time on Arc Pro B70 (us)
+README_GEMV_SHAPES = [("8B qkv", 4096, 6144, 14.39), ("8B o_proj", 4096, 4096, 10.35),
+                      ("8B gate_up", 4096, 24576, 47.23), ("8B down", 12288, 4096, 25.19),
+                      ("8B lm_head", 4096, 151680, 278.9), ("27B gate_up", 5120, 34816, 86.81),
+                      ("27B down", 17408, 5120, 42.76), ("27B in_proj_qkvz", 5120, 16384, 40.05),
+                      ("27B out_proj", 6144, 5120, 17.16), ("27B qkv", 5120, 14336, 35.54),
+                      ("27B lm_head", 5120, 248320, 572.5)]
+
+
+def gemv_shapes_measure(tl, dev, reps=20, cpu=True):
+    """M=1 fp16 int2 GEMV per shape of the reference's published table: back-to-back
+    launches of one shape in a CUDA graph over weight sets rotated past L2 (>= 400 MB),
+    us per call, weight GB/s and its fraction of the measured HBM peak; the o_proj shape
+    is configs[0] (M=1, K=N=4096, the host-reference config), timed also with the
+    reference's own host gold (oracle/_ref) on this host's cores."""
+    import torch
+    L = tl.lib()
+    peak, peak_kind = peaks()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    out = []
+    c1 = None
+    for name, K, N, b70 in README_GEMV_SHAPES:
+        wb = weight_bytes(K, N)
+        nsets = max(2, int(np.ceil(400e6 / wb)))
+        B0 = device_int2_words(K, N, gen, dev)
+        Bs = [B0] + [B0.view(-1)[torch.randperm(B0.numel(), generator=gen, device=dev)].view_as(B0).contiguous()
+                     for _ in range(nsets - 1)]
+        Ss = [(torch.rand(K // 128, N, generator=gen, device=dev) * 0.04 + 0.01).half() for _ in range(nsets)]
+        A = torch.randn(1, K, generator=gen, device=dev).half()
+        C = torch.empty(1, N, dtype=torch.float16, device=dev)
+        ws = tl.Workspace(dev, tl.gemv_workspace_size(1, N, K))
+
+        def call(i, cs):
+            check(tl, "ternocl_int2_upcvt", L.ternocl_int2_upcvt(A.data_ptr(), Bs[i % nsets].data_ptr(),
+                                                                 Ss[i % nsets].data_ptr(), C.data_ptr(), None, None,
+                                                                 1, N, K, 0, 0, 0, tl.ALGO_GEMV, ws.ptr(), ws.nbytes(),
+                                                                 cs))
+        torch.cuda.synchronize()
+        for i in range(nsets):
+            call(i, torch.cuda.current_stream(dev).cuda_stream)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for i in range(reps):
+                call(i, torch.cuda.current_stream(dev).cuda_stream)
+        gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        gbs = wb / (us * 1e-6) / 1e9
+        out.append({"shape": name, "K": K, "N": N, "us": us, "GBps": gbs, "frac": gbs / peak,
+                    "reference_b70_us": b70, "speedup_vs_reference_b70": b70 / us})
+        del gr, Bs, Ss, B0
+        torch.cuda.empty_cache()
+        if (K, N) == (4096, 4096):
+            c1 = {"metric": "M=1 int2 GEMV weight-stream HBM GB/s (configs[0]: K=N=4096, fp16)", "value": gbs,
+                  "unit": "GB/s", "us_per_call": us,
+                  "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                               "peak_kind": peak_kind}, "cpu_baseline": None}
+    if cpu and c1 is not None:
+        from oracle import api as orc
+        from ternocl_b200 import synth
+        rng = np.random.default_rng(0)
+        A0, B0, S0 = (synth.activations(rng, 1, 4096, 0), synth.pack_int2(synth.ternary(rng, 4096, 4096)),
+                      synth.scales(rng, 4096, 4096, 0))
+        kind = "reference" if orc.ref_available() else "port"
+        gold = orc.Ref.int2_gold if kind == "reference" else orc.int2_gold
+        n, el = cpu_loop(lambda: gold(A0, B0, S0, 1, 4096, 4096, 0), 3.0)
+        c1["cpu_baseline"] = {"value": n * weight_bytes(4096, 4096) / el / 1e9, "unit": "GB/s",
+                              "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), "kind": kind,
+                              "sample": "%d calls of compute_gold at M=1, K=N=4096, seed 0, %.1f s" % (n, el)}
+    return out, c1
+
+
 def moe_cpu_baseline(m, budget_s=8.0):
     """The MoE layer's token reference (int2_moe/prefill.cpp:291-310, double precision; the
     restatement, pinned through its parts) on the host cores: tokens/s over a bounded
@@ -1196,7 +1275,11 @@ def main():
                          "e2e": me2e, "cpu_baseline": mcpu}
         sec_int8 = int8_measure(tl, dev, steps=min(args.steps, 20), warmup=3, cpu=not args.no_cpu_baseline)
         sec_bitcos = bitcos_measure(tl, dev, steps=min(args.steps, 50), warmup=3, cpu=not args.no_cpu_baseline)
-        secondary = {"int8_prefill": sec_int8, "bitcos": sec_bitcos, "moe": secondary_moe,
+        gshapes, c1 = gemv_shapes_measure(tl, dev, cpu=not args.no_cpu_baseline)
+        secondary = {"int8_prefill": sec_int8, "bitcos": sec_bitcos, "moe": secondary_moe, "c1_host_config": c1,
+                     "gemv_shapes_m1": {"metric": "M=1 int2 fp16 GEMV per shape of the reference's published table "
+                                                  "(int2_fp16_upcvt/README.md), CUDA graph of back-to-back launches",
+                                        "unit": "GB/s", "shapes": gshapes},
                      "prefill": {"metric": "M=2048 int2 fp16 prefill TFLOP/s (tcgen05 GEMM)", "value": tf,
                                  "unit": "TFLOP/s", "ms_per_step": pms, "M": PREFILL_M, "shapes_KxN": SHAPES,
                                  "roofline": {"bound": "tensor", "achieved": tf, "peak": pk[0], "unit": "TFLOP/s",

@@ -95,13 +95,10 @@ int ternocl_device_error(int reset);
  *  TERNOCL_OPT_GEMV_IMPL (default 0 = chosen per M): the int2 decode GEMV used by
  *    ternocl_int2_upcvt at small M: 1 = fp16/bf16 MMA on decoded weights, 2 = integer
  *    MMA on int8 weights and exact fixed-point activations, one CTA per 32-column strip
- *    (M <= 4; the default there when no workspace is given), 3 = the same arithmetic in a
- *    persistent kernel fed by TMA with a stream-K split (M = 1; opt-in), 4 = the same
- *    arithmetic in one balanced wave of one CTA per SM, each warp streaming a contiguous
- *    range of (strip, 128-row group) units (M <= 4 with a workspace; opt-in: measured
- *    about 2x slower than 2 on the Llama-3-8B shapes).
- *  TERNOCL_OPT_GEMV_STAGES (default 0 = planned): units (1 KB of weights each) in flight
- *    per warp in the stream-K GEMV of GEMV_IMPL 4: 4, 6 or 8.
+ *    (M <= 4; the default there).  (Values 3 and 4, two measured-slower variants, were
+ *    removed: setting them returns -1.)
+ *  TERNOCL_OPT_GEMV_STAGES: reserved (it tuned one of the removed variants); setting it
+ *    returns -1.
  *  TERNOCL_OPT_PEER_TIMEOUT_MS (default 2000, 1..60000): how long the column-sharded GEMV
  *    (ternocl_int2_upcvt_allgather) waits for its peers before it gives up, sets bit 2 of
  *    ternocl_device_error and returns.

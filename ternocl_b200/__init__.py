@@ -18,7 +18,7 @@ OPT_GEMV_SPLIT = 3
 OPT_GEMV_WARPS = 4
 OPT_GEMM_PERSISTENT = 5
 OPT_GEMV_IMPL = 6
-OPT_GEMV_STAGES = 7
+OPT_GEMV_STAGES = 7  # reserved: setting it returns -1
 OPT_PEER_TIMEOUT_MS = 8
 
 

@@ -235,35 +235,7 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.stream = (cudaStream_t)stream;
     const int impl = options().gemv_impl;
-    if (M == 1 && !peer && impl == 3) {
-        // persistent TMA-streamed GEMV; its stream-K split needs the workspace
-        const size_t need = int2_gemv_p_workspace(N);
-        if (ws && ws_bytes >= need) {
-            if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
-            const int tiles = (N + 127) / 128;
-            a.ws_cnt = (unsigned *)ws;
-            a.ws_part = (float *)((char *)ws + round_up((size_t)tiles * 4, 256));
-        }
-        return cuda_status(int2_gemv_p_launch(a));
-    }
     const bool digit = M <= kGemvDigitMaxM && impl != 1;
-    if (digit && ws && impl == 4) {
-        // stream-K integer-MMA GEMV (opt-in): one balanced wave; small enough (<= ~110 KB
-        // of shared memory) that the next GEMV of the stream fits beside it on every SM
-        const int ctas = int2_gemv_s_ctas(M, N, K, sm_count());
-        int depth = options().gemv_stages;
-        if (!depth) {
-            depth = 8;
-            while (depth > 4 && int2_gemv_s_smem(M, K, depth) > kGemvCoresidentSmem) depth -= 2;
-        }
-        if (ctas >= 1 && int2_gemv_s_smem(M, K, depth) <= 227 * 1024 &&
-            int2_gemv_s_workspace(M, N, ctas) <= ws_bytes) {
-            if (!aligned(ws, 256)) return TERNOCL_ERR_ARG;
-            a.ws_cnt = (unsigned *)ws;
-            a.ws_part = (float *)((char *)ws + int2_gemv_s_cnt_bytes(N));
-            return cuda_status(int2_gemv_s_launch(a, ctas, depth));
-        }
-    }
     auto plan = [&](bool allow_ws) { return digit ? gemv_digit_plan(M, N, K, allow_ws) : gemv_plan(M, N, K, allow_ws); };
     GemvPlan p = plan(ws != nullptr);
     if (p.total() > ws_bytes) p = plan(false);
@@ -369,15 +341,9 @@ int ternocl_set_option(int option, int value) {
         return old;
     }
     if (option == TERNOCL_OPT_GEMV_IMPL) {
-        if (value < 0 || value > 4) return -1;
+        if (value < 0 || value > 2) return -1;
         const int old = options().gemv_impl;
         options().gemv_impl = value;
-        return old;
-    }
-    if (option == TERNOCL_OPT_GEMV_STAGES) {
-        if (value != 0 && value != 4 && value != 6 && value != 8) return -1;
-        const int old = options().gemv_stages;
-        options().gemv_stages = value;
         return old;
     }
     if (option == TERNOCL_OPT_PEER_TIMEOUT_MS) {
@@ -403,11 +369,6 @@ size_t ternocl_gemv_workspace_size(int M, int N, int K) {
     const size_t b = gemv_tc_plan(M, N, K, true).total(), c = gemv_i1_plan(M, N, K, true).total();
     if (b > need) need = b;
     if (c > need) need = c;
-    if (M == 1 && int2_gemv_p_workspace(N) > need) need = int2_gemv_p_workspace(N);
-    if (M <= kGemvDigitMaxM) {
-        const size_t s = int2_gemv_s_workspace(M, N, int2_gemv_s_ctas(M, N, K, sm_count()));
-        if (s > need) need = s;
-    }
     return need;
 }
 
@@ -424,8 +385,6 @@ int ternocl_device_error(int reset) {
     if (read_device_error_allgather(&t, reset) != cudaSuccess) return -1;
     v |= t;
     if (read_device_error_gemm_bitcos(&t, reset) != cudaSuccess) return -1;
-    v |= t;
-    if (read_device_error_gemv_p(&t, reset) != cudaSuccess) return -1;
     v |= t;
     if (read_device_error_moe_decode(&t, reset) != cudaSuccess) return -1;
     v |= t;

@@ -1,5 +1,5 @@
 // Integer-MMA pieces shared by the int2 GEMVs on int8 weights and fixed-point activation
-// digits (gemv_i2d.cu, gemv_i2p.cu, moe_decode.cu):
+// digits (gemv_i2d.cu, moe_decode.cu):
 //
 //  * weights: the 2-bit code of row j of a packed word sits in bits 2j..2j+1 of its byte,
 //    so (x << (6 - 2j)) & 0xC0C0C0C0 ("class j") leaves the codes of rows j, j+4, j+8, j+12

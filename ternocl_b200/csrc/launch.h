@@ -21,9 +21,7 @@ struct Options {
     int gemv_warps = 0;   // decode GEMV warps per CTA: 0 = planned per shape
     int gemm_persistent = 3;  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every prefill GEMM,
                               // 3 MoE grouped GEMMs with K <= 1024
-    int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA per strip (M <= 4),
-                              // 3 persistent (M = 1), 4 stream-K integer MMA (M <= 4)
-    int gemv_stages = 0;      // stream-K GEMV ring depth in units per warp: 0 = planned, 4, 6 or 8
+    int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA per strip (M <= 4)
     int peer_timeout_ms = 2000;  // limit of the column-sharded GEMV's wait for its peers
 };
 Options &options();
@@ -155,18 +153,6 @@ size_t int2_gemv_smem(int M, int K, int SK, int warps = 4);
 constexpr int kGemvDigitMaxM = 4;
 cudaError_t int2_gemv_d_launch(const GemvArgs &a);
 size_t int2_gemv_d_smem(int M, int K, int SK, int warps);
-// stream-K int2 GEMV on integer MMAs (gemv_i2s.cu, M <= 4): one wave of <= `sms` CTAs of 8
-// warps over balanced unit ranges; needs a workspace [strip counters | split-strip partials]
-int int2_gemv_s_ctas(int M, int N, int K, int sms);
-size_t int2_gemv_s_smem(int M, int K, int depth);
-size_t int2_gemv_s_cnt_bytes(int N);
-size_t int2_gemv_s_workspace(int M, int N, int ctas);
-cudaError_t int2_gemv_s_launch(const GemvArgs &a, int ctas, int depth);
-// persistent TMA-streamed int2 GEMV for M = 1 (gemv_i2p.cu); a.ws_part / a.ws_cnt (or null)
-// hold its stream-K partials and tile counters
-cudaError_t int2_gemv_p_launch(const GemvArgs &a);
-size_t int2_gemv_p_workspace(int N);
-cudaError_t read_device_error_gemv_p(unsigned *out, int reset);
 // tcgen05 / TMEM decode GEMV (gemv_tc.cu): 128 columns and tc_gemv_rows(M) rows per CTA
 int tc_gemv_rows(int M);
 size_t int2_gemv_tc_smem(int M, int K, int SK);

@@ -27,17 +27,15 @@ def run(tl, c, M, K, N, bf16, postop, out_f32, algo, ws=None):
 
 
 # GEMV implementations: fp16/bf16 mma.sync on decoded weights, integer mma.sync on int8
-# weights and fixed-point activation digits (M <= 4) per 32-column strip, the same as one
-# balanced stream-K wave (M <= 4 with a workspace), the persistent TMA-fed variant
-# (M = 1; larger M fall back), tcgen05/TMEM
-ALGOS = ["f16", "digit", "stream", "persist", "tmem"]
+# weights and fixed-point activation digits (M <= 4) per 32-column strip, tcgen05/TMEM
+ALGOS = ["f16", "digit", "tmem"]
 
 
 @pytest.fixture
 def gemv_algo(request, tl):
     """Maps an ALGOS name to (algo argument, implementation option) for the test body."""
     def select(name):
-        impl = {"f16": 1, "digit": 2, "stream": 4, "persist": 3, "tmem": 0}[name]
+        impl = {"f16": 1, "digit": 2, "tmem": 0}[name]
         old = tl.set_option(tl.OPT_GEMV_IMPL, impl)
         request.addfinalizer(lambda: tl.set_option(tl.OPT_GEMV_IMPL, old))
         return tl.ALGO_GEMV_TMEM if name == "tmem" else tl.ALGO_GEMV
@@ -122,14 +120,13 @@ def test_decode_bit_exact(cuda, tl, gemv_algo, algo):
     assert np.array_equal(out, np.array([0, 1, -2, -1], np.float32)[codes])
 
 
-@pytest.mark.parametrize("impl", ["digit", "stream"])
+@pytest.mark.parametrize("impl", ["digit"])
 def test_digit_onehot_bit_exact(cuda, tl, gemv_algo, impl):
     # the integer-MMA GEMVs at M = 4 with one-hot activation rows: C[i, n] is the decoded
-    # weight of row k_i exactly (every code and every position of a 16-row word); the
-    # stream-K shape gives every warp one unit, so every strip is summed from 8 pieces
+    # weight of row k_i exactly (every code and every position of a 16-row word)
     from ternocl_b200 import synth
     algo = gemv_algo(impl)
-    K, N = (256, 64) if impl == "digit" else (1024, 256)
+    K, N = 256, 64
     rng = np.random.default_rng(18)
     B = rng.integers(0, 1 << 32, size=(K // 16, N), dtype=np.uint64).astype(np.uint32)
     S = synth.to_dt(np.ones((K // 128, N)), 0)
@@ -144,7 +141,7 @@ def test_digit_onehot_bit_exact(cuda, tl, gemv_algo, impl):
         assert np.array_equal(out, want[k0:k0 + 4]), k0
 
 
-@pytest.mark.parametrize("impl", ["digit", "stream"])
+@pytest.mark.parametrize("impl", ["digit"])
 @pytest.mark.parametrize("bf16", [0, 1])
 def test_digit_outliers_and_zero_rows(cuda, tl, gemv_algo, bf16, impl):
     # rows with a large outlier (the fixed-point step follows the row maximum), a row of
@@ -168,7 +165,7 @@ def test_digit_outliers_and_zero_rows(cuda, tl, gemv_algo, bf16, impl):
     check_output(out, int2_gold_out(c, M, K, N, bf16, 0, True), bf16, True, "digit outliers fp32")
 
 
-@pytest.mark.parametrize("impl", ["digit", "stream"])
+@pytest.mark.parametrize("impl", ["digit"])
 def test_digit_row_max_positions(cuda, tl, gemv_algo, impl):
     # the fixed-point exponent follows each row's largest |A|: put it in every position of
     # a 16-byte load (low and high halves of each 32-bit pair) with larger values elsewhere

@@ -127,12 +127,23 @@ static GemvPlan gemv_plan(int M, int N, int K, bool allow_ws) {
 // the extra CTAs give), and 8 warps per CTA beat 16 on K = 4096 (4 once the grid holds
 // >= 4 CTAs per SM): 4096x4096 6.7 -> 4.6 us, 4096x6144 6.6 -> 5.8 us, 14336x4096 9.6
 // -> 9.4 us.
+//
+// Re-measured over the shapes of the reference's published table (int2_fp16_upcvt/README.md,
+// CUDA graphs of one shape, M = 1): with 1-2 strips per SM a long K (>= 64 groups) pays
+// for a two-way split (17408x5120 14.5 -> 12.3 us).  With fewer strips than SMs, 16 warps
+// per CTA measured faster per shape (4096x4096 4.55 -> 3.98 us, 14336x4096 10.58 -> 9.14)
+// but slowed the bench's four-shape sequence (32.3 -> 33.8 us per step: the larger CTAs
+// overlap less with the neighbouring GEMVs), so 8 stay.
 static GemvPlan gemv_digit_plan(int M, int N, int K, bool allow_ws) {
     const int G = K / kGS, sms = sm_count();
     const long long tiles = (long long)((N + 31) / 32) * ((M + 3) / 4);
-    int sk = options().gemv_split ? options().gemv_split : (2 * tiles < sms ? 2 : 1);
+    int sk = 1;
+    const int dwarps = tiles >= 4LL * sms ? 4 : 8;
+    if (2 * tiles < sms) sk = 2;
+    else if (tiles >= sms && tiles < 2LL * sms && G >= 64) sk = 2;
+    if (options().gemv_split) sk = options().gemv_split;
     if (sk > G) sk = G;
-    const int warps = options().gemv_warps ? options().gemv_warps : (tiles >= 4LL * sms ? 4 : 8);
+    const int warps = options().gemv_warps ? options().gemv_warps : dwarps;
     GemvPlan p;
     p.SK = sk;
     while (p.SK < G && int2_gemv_d_smem(M, K, p.SK, warps) > kGemvSmemBudget) ++p.SK;

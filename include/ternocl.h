@@ -9,7 +9,8 @@
  *
  * Conventions
  *  - All tensor pointers are caller-owned DEVICE pointers; nothing here allocates
- *    device memory.  16-bit tensors (A, S, SA, SB, C, Other, Bias, RW) are raw
+ *    device memory, except ternocl_int2_int8 with qmode 1 on its tensor-core GEMM
+ *    (stream-ordered scratch, see there).  16-bit tensors (A, S, SA, SB, C, Other, Bias, RW) are raw
  *    fp16 or bf16 bits (`dtype`); with out_f32 the output C and Bias are fp32.
  *  - Other/Bias may be NULL when the epilogue does not read them.
  *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
@@ -218,7 +219,12 @@ int ternocl_int8_quant_a(const void *A, void *SA, int8_t *Aq, int M, int K, int 
  * (int2_int8_dpas.cl:213-215, 316-318):
  *   C[m,n] = DT(epi( sum_g float(sum_{k in g} q[m,k] * code(B[k,n])) * (SB[g,n] * (1/SA[g,m])) ))
  * with int32 dot products per 128-group.  qmode 0: reads the int8 Aq written by
- * ternocl_int8_quant_a; qmode 1: quantises A in the kernel from SA (Aq unused).
+ * ternocl_int8_quant_a; qmode 1: quantises A from SA, q = sat_int8(rint(A * SA)) (Aq
+ * unused; may be a dummy buffer, as the reference driver passes in qmode 1).  The
+ * tensor-core GEMM (algo GEMM, or AUTO from M >= 64; SA 16-byte aligned) runs qmode 1 as
+ * one quantisation pass into M x K bytes of stream-ordered scratch from a pool of the
+ * library that keeps its pages (cudaMallocFromPoolAsync / cudaFreeAsync on `stream`;
+ * capturable), then the int8 GEMM: the codes, and so C, equal qmode 0's.
  * B as ternocl_int2_upcvt (codes read as 2-bit two's complement). */
 int ternocl_int2_int8(const void *A, const int8_t *Aq, const void *SA, const uint32_t *B,
                       const void *SB, void *C, const void *Other, const void *Bias, int M, int N,

@@ -1,6 +1,8 @@
 // extern "C" entry points of libternocl: argument validation (the reference's
 // host-side checks, e.g. int2_fp16_upcvt/main.cpp:159), workspace planning and
-// dispatch to the kernel families.  No entry point allocates device memory.
+// dispatch to the kernel families.  No entry point allocates device memory except
+// ternocl_int2_int8 with qmode 1 on the tensor-core GEMM, which takes its M x K int8
+// codes from a stream-ordered pool (scratch_alloc below).
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -56,9 +58,6 @@ static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // shared memory a GEMV CTA may use (activation staging + weight ring)
 constexpr size_t kGemvSmemBudget = 100 * 1024;
-// shared memory of a one-CTA-per-SM GEMV that leaves room on the SM for the next
-// kernel's CTA of the same size (228 KB per SM, 1 KB reserved per CTA)
-constexpr size_t kGemvCoresidentSmem = 112 * 1024;
 constexpr int kMaxClusterSK = 8;  // portable thread-block cluster size
 
 // Split-K plan of a decode GEMV whose CTAs cover `cols` columns x `rows` activation
@@ -534,6 +533,38 @@ int ternocl_int8_quant_a(const void *A, void *SA, int8_t *Aq, int M, int K, int 
     return cuda_status(quant_a_launch(A, SA, Aq, M, K, dtype, (cudaStream_t)stream));
 }
 
+// Stream-ordered scratch of the library, one pool per device that keeps what it has
+// mapped (release threshold = max), so a steady caller maps no pages per call; under
+// stream capture the allocation becomes a graph memory node.  The memory is back in the
+// pool once the stream passes the matching cudaFreeAsync.
+static cudaError_t scratch_alloc(void **ptr, size_t bytes, cudaStream_t s) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!pools[dev]) {
+            cudaMemPoolProps props;
+            std::memset(&props, 0, sizeof props);
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = dev;
+            cudaMemPool_t pool;
+            if ((e = cudaMemPoolCreate(&pool, &props)) != cudaSuccess) return e;
+            uint64_t keep = ~0ull;
+            if ((e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess) {
+                cudaMemPoolDestroy(pool);
+                return e;
+            }
+            pools[dev] = pool;
+        }
+    }
+    return cudaMallocFromPoolAsync(ptr, bytes, pools[dev], s);
+}
+
 int ternocl_int2_int8(const void *A, const int8_t *Aq, const void *SA, const uint32_t *B,
                       const void *SB, void *C, const void *Other, const void *Bias, int M, int N,
                       int K, int dtype, int postop, int out_f32, int qmode, int algo, void *stream) {
@@ -549,13 +580,28 @@ int ternocl_int2_int8(const void *A, const int8_t *Aq, const void *SA, const uin
     a.M = M; a.N = N; a.K = K; a.dtype = dtype; a.postop = postop; a.out_f32 = out_f32;
     a.Aq = Aq; a.SA = SA; a.qmode = qmode;
     a.stream = (cudaStream_t)stream;
-    // the tensor-core GEMM reads the int8 codes (qmode 0) and copies the scale rows in
-    // 16-byte units; qmode 1 quantises inside the GEMV kernel, which also serves any M in
-    // 8-row blocks
+    // the tensor-core GEMM reads int8 codes and copies the scale rows in 16-byte units.
+    // qmode 0: the caller's Aq.  qmode 1 (the reference's default scheme: quantise with the
+    // caller's SA inside the GEMM, int2_int8_dpas.cl:283-290): one pass quantises A into
+    // stream-ordered scratch, so each row block is quantised once rather than once per
+    // 128-column tile (168 times at N = 21504); the codes are the in-kernel ones bit for
+    // bit.  The GEMV kernel quantises in its own loads and serves any M in 8-row blocks.
     const bool sa16 = aligned(SA, 16);
-    if (algo == TERNOCL_ALGO_GEMM && qmode == 0 && !sa16) return TERNOCL_ERR_ARG;
-    if (qmode == 0 && sa16 && (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM)))
-        return cuda_status(int8_gemm_tc_launch(a));
+    if (algo == TERNOCL_ALGO_GEMM && !sa16) return TERNOCL_ERR_ARG;
+    if (sa16 && (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM))) {
+        if (qmode == 0) return cuda_status(int8_gemm_tc_launch(a));
+        if (!aligned(A, 8)) return TERNOCL_ERR_ARG;
+        void *q = nullptr;
+        cudaError_t e = scratch_alloc(&q, (size_t)M * K, a.stream);
+        if (e != cudaSuccess) return cuda_status(e);
+        e = quant_apply_launch(A, SA, (int8_t *)q, M, K, dtype, a.stream);
+        if (e == cudaSuccess) {
+            a.Aq = (const int8_t *)q;
+            e = int8_gemm_tc_launch(a);
+        }
+        const cudaError_t fe = cudaFreeAsync(q, a.stream);
+        return cuda_status(e != cudaSuccess ? e : fe);
+    }
     // no workspace in this signature: split-K stays within one thread-block cluster
     const GemvPlan p = gemv_i8_plan(M, N, K, false);
     if (int8_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;

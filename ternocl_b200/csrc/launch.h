@@ -137,6 +137,8 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 
 // Kernel-family entry points (one per .cu file).
 cudaError_t quant_a_launch(const void *A, void *SA, int8_t *Aq, int M, int K, int dtype, cudaStream_t s);
+// Aq = sat_int8(rint(A * SA)) with the caller's SA (no scale computed)
+cudaError_t quant_apply_launch(const void *A, const void *SA, int8_t *Aq, int M, int K, int dtype, cudaStream_t s);
 cudaError_t group_dots_launch(const int8_t *Aq, const uint32_t *B, int32_t *D, int M, int N, int K,
                               cudaStream_t s);
 cudaError_t int8_gemv_launch(const GemvArgs &a);

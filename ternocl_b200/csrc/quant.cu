@@ -18,8 +18,11 @@ namespace {
 
 constexpr float kFltEpsilon = 1.1920928955078125e-07f;
 
-// One warp per (row m, group g): lane l holds A[m, 128g + 4l .. 4l+3].
-template <class DT>
+// One warp per (row m, group g): lane l holds A[m, 128g + 4l .. 4l+3].  SCALE: compute
+// SA[g, m] from the group's absmax and write it (quant_a); otherwise read the caller's SA
+// and only quantise (the QMODE 1 scheme's in-GEMM quantisation, int2_int8_dpas.cl:128-160,
+// run once per row block instead of once per column tile).
+template <class DT, bool SCALE>
 __global__ void __launch_bounds__(256) quant_a_kernel(const uint16_t *__restrict__ A, uint16_t *__restrict__ SA,
                                                      int8_t *__restrict__ Aq, int M, int K, int ldsa) {
     pdl_wait();
@@ -31,12 +34,17 @@ __global__ void __launch_bounds__(256) quant_a_kernel(const uint16_t *__restrict
     const uint2 raw = *reinterpret_cast<const uint2 *>(A + off);
     float a[4] = {DT::tof((uint16_t)(raw.x & 0xffffu)), DT::tof((uint16_t)(raw.x >> 16)),
                   DT::tof((uint16_t)(raw.y & 0xffffu)), DT::tof((uint16_t)(raw.y >> 16))};
-    float mx = fmaxf(fmaxf(fabsf(a[0]), fabsf(a[1])), fmaxf(fabsf(a[2]), fabsf(a[3])));
+    uint16_t sh;
+    if (SCALE) {
+        float mx = fmaxf(fmaxf(fabsf(a[0]), fabsf(a[1])), fmaxf(fabsf(a[2]), fabsf(a[3])));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    // max(FLT_EPSILON, absmax), then the correctly rounded quotient, then RNE to DT
-    const uint16_t sh = DT::fromf(__fdiv_rn(127.0f, fmaxf(mx, kFltEpsilon)));
-    if (lane == 0) SA[(size_t)g * ldsa + m] = sh;
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // max(FLT_EPSILON, absmax), then the correctly rounded quotient, then RNE to DT
+        sh = DT::fromf(__fdiv_rn(127.0f, fmaxf(mx, kFltEpsilon)));
+        if (lane == 0) SA[(size_t)g * ldsa + m] = sh;
+    } else {
+        sh = SA[(size_t)g * ldsa + m];
+    }
     if (Aq) {
         const float sa = DT::tof(sh);
         uint32_t packed = 0;
@@ -79,10 +87,21 @@ cudaError_t quant_a_launch(const void *A, void *SA, int8_t *Aq, int M, int K, in
     dim3 grid((warps + 7) / 8);
     const int ldsa = (M + 31) & ~31;
     if (dtype == TERNOCL_BF16)
-        return launch_kernel(quant_a_kernel<BF16>, grid, dim3(256), 0, s, (const uint16_t *)A, (uint16_t *)SA, Aq,
-                             M, K, ldsa);
-    return launch_kernel(quant_a_kernel<F16>, grid, dim3(256), 0, s, (const uint16_t *)A, (uint16_t *)SA, Aq, M, K,
-                         ldsa);
+        return launch_kernel(quant_a_kernel<BF16, true>, grid, dim3(256), 0, s, (const uint16_t *)A, (uint16_t *)SA,
+                             Aq, M, K, ldsa);
+    return launch_kernel(quant_a_kernel<F16, true>, grid, dim3(256), 0, s, (const uint16_t *)A, (uint16_t *)SA, Aq,
+                         M, K, ldsa);
+}
+
+cudaError_t quant_apply_launch(const void *A, const void *SA, int8_t *Aq, int M, int K, int dtype, cudaStream_t s) {
+    const int warps = M * (K / kGS);
+    dim3 grid((warps + 7) / 8);
+    const int ldsa = (M + 31) & ~31;
+    uint16_t *sa = (uint16_t *)const_cast<void *>(SA);  // read only (SCALE = false)
+    if (dtype == TERNOCL_BF16)
+        return launch_kernel(quant_a_kernel<BF16, false>, grid, dim3(256), 0, s, (const uint16_t *)A, sa, Aq, M, K,
+                             ldsa);
+    return launch_kernel(quant_a_kernel<F16, false>, grid, dim3(256), 0, s, (const uint16_t *)A, sa, Aq, M, K, ldsa);
 }
 
 cudaError_t group_dots_launch(const int8_t *Aq, const uint32_t *B, int32_t *D, int M, int N, int K,

@@ -6,8 +6,9 @@ reference's host gold, compiled from its sources or restated and pinned to it).
   every epilogue on the largest shape (common/epilogue.hpp:50-67).
 * C3, the s8 x s2 prefill at 27B-like shapes, M = 1, 512, 2048 (bf16): quant_a's SA and
   the int8 codes bit for bit, the outputs on 16 sampled rows (each output row depends on
-  its own activation row only, int2_via_int2_x_int8_dpas/main.cpp:94-121), and the int32
-  group dots bit for bit on a column slice.
+  its own activation row only, int2_via_int2_x_int8_dpas/main.cpp:94-121), the int32
+  group dots bit for bit on a column slice, and qmode 1 (quantise from SA in the GEMM,
+  the driver's default) equal to qmode 0 bit for bit.
 * C4, BITCOS with the Hadamard pre-transform, K = 5376, N = 21504, z = 0.2/0.35/0.5,
   M = 1, 8, 512 (HB = 256: 1024 does not divide 5376): the transform bit for bit and the
   outputs against bitcos_fp16_upcvt/main.cpp:64-86 (sampled rows at M = 512).
@@ -127,6 +128,10 @@ def test_c3_int8_prefill(cuda, tl, K, N, M):
     Bs = np.ascontiguousarray(B[:, n0:n0 + ns])
     D = tl.int2_int8_group_dots(dev_any(Aq_rows), dev_u32(Bs)).cpu().numpy()
     assert np.array_equal(D, orc.int8_group_dots(Q_gold, Bs, r, K, ns)), "group dots"
+    # qmode 1 (the reference driver's default: scales only, quantise in the GEMM) gives
+    # the same bits as qmode 0 on every path
+    out1 = host_dt(tl.int2_int8(dA, dB, dev_dt(SB, bf16), SA, qmode=1))
+    assert np.array_equal(out1.view(np.uint16), out.view(np.uint16)), "qmode 1 vs qmode 0"
     assert tl.device_error() == 0
 
 

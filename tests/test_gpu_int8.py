@@ -204,3 +204,53 @@ def test_gemm_matches_gemv_kernel(cuda, tl):
     v = host_dt(tl.int2_int8(*args, Aq=Aq, qmode=0, algo=tl.ALGO_GEMV, out_f32=True))
     # the int32 dots are equal; only the fp32 order of the group sums differs
     assert rel_err(g, v, F32_FLOOR) <= F32_REL_TOL
+
+
+# ---- qmode 1 on the tensor-core GEMM (the reference driver's default scheme: scale
+# pre-kernel, quantise in the GEMM; int2_via_int2_x_int8_dpas/main.cpp:58, 316): one pass
+# quantises A with the caller's SA into pooled scratch, then the same int8 GEMM, so the
+# output is qmode 0's bit for bit
+@pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("M,K,N", [(64, 128, 128), (100, 256, 272), (300, 1024, 400)])
+def test_gemm_qmode1_equals_qmode0(cuda, tl, M, K, N, bf16):
+    import torch
+    c = case(1300 + M + K + N, M, K, N, bf16)
+    A = dev_dt(c["A"], bf16)
+    B, SB = dev_u32(c["B"]), dev_dt(c["SB"], bf16)
+    SA, Aq = tl.int8_quant_a(A)
+    SA1, none = tl.int8_quant_a(A, write_q=False)  # the scale pre-kernel alone
+    assert none is None and torch.equal(SA1, SA)
+    g0 = host_dt(tl.int2_int8(A, B, SB, SA, Aq=Aq, qmode=0, algo=tl.ALGO_GEMM))
+    dummy = torch.zeros(64, dtype=torch.int8, device="cuda")  # the 64-byte Aq of qmode 1
+    for algo in (tl.ALGO_GEMM, tl.ALGO_AUTO):
+        g1 = host_dt(tl.int2_int8(A, B, SB, SA1, Aq=dummy, qmode=1, algo=algo))
+        assert np.array_equal(g1.view(np.uint16), g0.view(np.uint16)), "qmode 1 algo %d" % algo
+    assert torch.count_nonzero(dummy).item() == 0
+    gold = gold_out(c, M, K, N, bf16, 0, False)
+    check_output(g0, gold, bf16, False, "s8xs2 gemm qmode=1 M=%d K=%d N=%d" % (M, K, N))
+    assert tl.device_error() == 0
+
+
+def test_gemm_qmode1_in_graph(cuda, tl):
+    # the scratch allocation is stream-ordered, so the call captures into a CUDA graph
+    import torch
+    M, K, N = 128, 512, 256
+    c = case(77, M, K, N, 0)
+    A = dev_dt(c["A"], 0)
+    B, SB = dev_u32(c["B"]), dev_dt(c["SB"], 0)
+    SA, _ = tl.int8_quant_a(A, write_q=False)
+    ref = host_dt(tl.int2_int8(A, B, SB, SA, qmode=1, algo=tl.ALGO_GEMM))
+    out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            tl.int2_int8(A, B, SB, SA, qmode=1, algo=tl.ALGO_GEMM, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(2):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(host_dt(out).view(np.uint16), ref.view(np.uint16))
+    del g

@@ -103,6 +103,10 @@ int ternocl_device_error(int reset);
  *  TERNOCL_OPT_PEER_TIMEOUT_MS (default 2000, 1..60000): how long the column-sharded GEMV
  *    (ternocl_int2_upcvt_allgather) waits for its peers before it gives up, sets bit 2 of
  *    ternocl_device_error and returns.
+ *  TERNOCL_OPT_BITCOS_GEMV (default 0): the BITCOS decode GEMV of ternocl_bitcos_upcvt:
+ *    0 = at M <= 8 the persistent kernel (one CTA per SM over whole-K strips of 32
+ *    columns; LS and SR are not read), else the K-sliced kernel; 1 = always the K-sliced
+ *    kernel (the reference's LS split with slice ranks).
  * Returns the previous value, or -1 for an unknown option or value. */
 typedef enum {
     TERNOCL_OPT_PDL = 1,
@@ -112,7 +116,8 @@ typedef enum {
     TERNOCL_OPT_GEMM_PERSISTENT = 5,
     TERNOCL_OPT_GEMV_IMPL = 6,
     TERNOCL_OPT_GEMV_STAGES = 7,
-    TERNOCL_OPT_PEER_TIMEOUT_MS = 8
+    TERNOCL_OPT_PEER_TIMEOUT_MS = 8,
+    TERNOCL_OPT_BITCOS_GEMV = 9
 } ternocl_option;
 int ternocl_set_option(int option, int value);
 

@@ -20,6 +20,7 @@ OPT_GEMM_PERSISTENT = 5
 OPT_GEMV_IMPL = 6
 OPT_GEMV_STAGES = 7  # reserved: setting it returns -1
 OPT_PEER_TIMEOUT_MS = 8
+OPT_BITCOS_GEMV = 9
 
 
 def _torch():

@@ -356,6 +356,12 @@ int ternocl_set_option(int option, int value) {
         options().gemv_impl = value;
         return old;
     }
+    if (option == TERNOCL_OPT_BITCOS_GEMV) {
+        if (value < 0 || value > 1) return -1;
+        const int old = options().bitcos_gemv;
+        options().bitcos_gemv = value;
+        return old;
+    }
     if (option == TERNOCL_OPT_PEER_TIMEOUT_MS) {
         if (value < 1 || value > 60000) return -1;
         const int old = options().peer_timeout_ms;
@@ -397,6 +403,8 @@ int ternocl_device_error(int reset) {
     if (read_device_error_gemm_bitcos(&t, reset) != cudaSuccess) return -1;
     v |= t;
     if (read_device_error_moe_decode(&t, reset) != cudaSuccess) return -1;
+    v |= t;
+    if (read_device_error_gemv_bitcos_p(&t, reset) != cudaSuccess) return -1;
     v |= t;
     return (int)v;
 }
@@ -476,6 +484,9 @@ int ternocl_bitcos_upcvt(const void *A, const uint32_t *B, const void *S, const 
     // M >= kGemmMinM)
     if (algo == TERNOCL_ALGO_GEMM || (algo == TERNOCL_ALGO_AUTO && M >= kGemmMinM))
         return cuda_status(bitcos_gemm_tc_launch(a));
+    // M <= 8: one CTA per SM over whole-K strips (no split, so LS and SR are not read)
+    if (options().bitcos_gemv == 0 && bitcos_gemv_p_smem(M, K) > 0)
+        return cuda_status(bitcos_gemv_p_launch(a, sm_count()));
     // no workspace in this signature: split-K stays within one thread-block cluster
     const GemvPlan p = gemv_bitcos_plan(M, N, K, false);
     if (bitcos_gemv_smem(M, K, p.SK) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;

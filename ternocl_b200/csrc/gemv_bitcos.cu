@@ -235,11 +235,15 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
         scnt[c] = ok ? (r >> 5) + 2 - wlo : 0u;  // windows read words rank/32 and rank/32 + 1
     }
     __syncthreads();
-    // 4. the sign words of each column's range (contiguous in the stream, 4-byte copies)
+    // 4. the sign words of each column's range, contiguous in the stream: warp w copies
+    //    columns w, w + 4, ..., its lanes consecutive words (4-byte copies: a column's
+    //    first word has no alignment)
     const uint32_t *signs = B + bw + N;
-    for (int idx = tid; idx < 32 * cap; idx += kThreads) {
-        const int c = idx / cap, i = idx - c * cap;
-        if ((uint32_t)i < scnt[c]) cp_async4(ssg + idx, signs + soff[c] + swlo[c] + i);
+    for (int c = warp; c < 32; c += gemv::kWarps) {
+        const uint32_t cnt = scnt[c];
+        const uint32_t *src = signs + soff[c] + swlo[c];
+        uint32_t *dst = ssg + c * cap;
+        for (uint32_t i = lane; i < cnt; i += 32) cp_async4(dst + i, src + i);
     }
     // 5. activations, 16-byte unit u stored at u ^ (((u >> 3) & 1) << 1)
     pdl_wait();

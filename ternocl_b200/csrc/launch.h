@@ -23,6 +23,7 @@ struct Options {
                               // 3 MoE grouped GEMMs with K <= 1024
     int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA per strip (M <= 4)
     int peer_timeout_ms = 2000;  // limit of the column-sharded GEMV's wait for its peers
+    int bitcos_gemv = 0;         // BITCOS decode GEMV: 0 persistent strip kernel where it applies, 1 K-sliced
 };
 Options &options();
 
@@ -144,6 +145,10 @@ cudaError_t group_dots_launch(const int8_t *Aq, const uint32_t *B, int32_t *D, i
 cudaError_t int8_gemv_launch(const GemvArgs &a);
 cudaError_t int1_gemv_launch(const GemvArgs &a);
 cudaError_t bitcos_gemv_launch(const GemvArgs &a);
+// persistent strip-pipelined BITCOS GEMV (gemv_bitcos_p.cu): M <= 8; smem 0 = not applicable
+size_t bitcos_gemv_p_smem(int M, int K);
+cudaError_t bitcos_gemv_p_launch(const GemvArgs &a, int sms);
+cudaError_t read_device_error_gemv_bitcos_p(unsigned *out, int reset);
 cudaError_t hadamard_launch(const void *x, const int8_t *signs, void *y, int rows, int K, int hb, int use_signs,
                             int dtype, cudaStream_t st);
 size_t bitcos_gemv_smem(int M, int K, int SK, int had_hb = 0);

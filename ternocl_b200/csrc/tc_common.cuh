@@ -261,5 +261,22 @@ static inline cudaError_t make_map_sw128(CUtensorMap *map, const void *base, CUt
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// Row-major [rows, cols] matrix of `type` (elem_bytes each) as unswizzled boxes of
+// box_rows x box_cols (box_cols * elem_bytes a multiple of 16), landing row-major and
+// dense in shared memory; reads past the matrix give 0.
+static inline cudaError_t make_map_plain(CUtensorMap *map, const void *base, CUtensorMapDataType type,
+                                         int elem_bytes, int rows, int cols, int box_rows, int box_cols) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * (cuuint64_t)elem_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, type, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace tc
 }  // namespace ternocl

@@ -34,6 +34,15 @@ def gold_out(c, M, K, N, bf16, postop, out_f32):
     return orc.epilogue(postop, out_f32, acc, c["other"], c["bias"], M, N, bf16)
 
 
+@pytest.fixture(params=[0, 1], ids=["strip", "ksliced"])
+def gemv_impl(request, tl):
+    """Both decode GEMVs: the persistent whole-K strip kernel (default at M <= 8) and
+    the K-sliced kernel of the reference's LS split (TERNOCL_OPT_BITCOS_GEMV = 1)."""
+    old = tl.set_option(tl.OPT_BITCOS_GEMV, request.param)
+    yield request.param
+    tl.set_option(tl.OPT_BITCOS_GEMV, old)
+
+
 def run(tl, c, K, N, bf16, ls, postop=0, out_f32=False, algo=0):
     import torch
     A, B, S = dev_dt(c["A"], bf16), dev_words(c["buf"]), dev_dt(c["S"], bf16)
@@ -50,7 +59,7 @@ def run(tl, c, K, N, bf16, ls, postop=0, out_f32=False, algo=0):
 @pytest.mark.parametrize("z", [0.2, 0.35, 0.5])
 @pytest.mark.parametrize("M,K,N,ls", [(1, 5376, 512, 4), (1, 5376, 512, 1), (8, 1024, 256, 2), (3, 256, 48, 4),
                                       (1, 4096, 4096, 4), (13, 512, 128, 1), (2, 5376, 272, 7)])
-def test_gemv_parity(cuda, tl, M, K, N, ls, z, bf16):
+def test_gemv_parity(cuda, tl, gemv_impl, M, K, N, ls, z, bf16):
     c = case(tl, 500 + M + K + N + int(100 * z), M, K, N, z, bf16)
     gold = gold_out(c, M, K, N, bf16, 0, False)
     check_output(run(tl, c, K, N, bf16, ls), gold, bf16, False,
@@ -58,7 +67,7 @@ def test_gemv_parity(cuda, tl, M, K, N, ls, z, bf16):
 
 
 @pytest.mark.parametrize("z", [0.0, 0.95, 1.0])
-def test_gemv_density_extremes(cuda, tl, z):
+def test_gemv_density_extremes(cuda, tl, gemv_impl, z):
     # all non-zero, almost all zero, and an empty sign plane
     M, K, N = 2, 2048, 384
     c = case(tl, 41, M, K, N, z, 0)
@@ -72,7 +81,7 @@ def test_gemv_density_extremes(cuda, tl, z):
 @pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("postop", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("out_f32", [False, True])
-def test_gemv_epilogues(cuda, tl, bf16, postop, out_f32):
+def test_gemv_epilogues(cuda, tl, gemv_impl, bf16, postop, out_f32):
     M, K, N = 3, 2048, 512
     c = case(tl, 70 + postop, M, K, N, 0.35, bf16, postop, out_f32)
     gold = gold_out(c, M, K, N, bf16, postop, out_f32)
@@ -80,7 +89,7 @@ def test_gemv_epilogues(cuda, tl, bf16, postop, out_f32):
                  "postop=%d out_f32=%d" % (postop, out_f32))
 
 
-def test_decode_bit_exact(cuda, tl):
+def test_decode_bit_exact(cuda, tl, gemv_impl):
     # A = identity: C[k, n] = code(k, n) * S[k/128, n] exactly (one non-zero term),
     # so the output is the decoded weight matrix, compared with bitcos_decode_col
     K, N = 512, 96
@@ -93,7 +102,7 @@ def test_decode_bit_exact(cuda, tl):
         assert np.array_equal(out, orc.bitcos_decode(buf, K, N).T.astype(np.float32)), ls
 
 
-def test_gemv_golden(cuda, tl):
+def test_gemv_golden(cuda, tl, gemv_impl):
     d = np.load(GOLDEN)
     for zk in ("z35", "z05", "z95"):
         buf = d["bitcos_%s_buf" % zk]
@@ -105,6 +114,20 @@ def test_gemv_golden(cuda, tl):
             c = dict(A=A, buf=buf, S=S, other=None, bias=None)
             for ls in (1, 2, 4):
                 check_output(run(tl, c, K, N, bf16, ls), gold, bf16, False, "%s %s ls=%d" % (zk, dt, ls))
+
+
+@pytest.mark.parametrize("M,N", [(1, 21504), (8, 5136)])
+def test_gemv_strip_kernel_many_strips(cuda, tl, M, N):
+    # more strips than SMs (each CTA walks several, through its staged ring), a last
+    # strip of 16 columns (N % 32 == 16), and the last column's run (no offset follows
+    # it); deterministic over reruns
+    K = 5376
+    c = case(tl, 900 + M, M, K, N, 0.35, 0)
+    gold = gold_out(c, M, K, N, 0, 0, False)
+    first = run(tl, c, K, N, 0, 4)
+    check_output(first, gold, 0, False, "strip kernel M=%d N=%d" % (M, N))
+    assert np.array_equal(run(tl, c, K, N, 0, 4).view(np.uint16), first.view(np.uint16))
+    assert tl.device_error() == 0
 
 
 def test_shape_errors(cuda, tl):

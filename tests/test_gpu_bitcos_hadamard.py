@@ -25,9 +25,13 @@ def case(tl, seed, M, K, N, z, bf16):
 
 @pytest.fixture
 def split(tl):
+    # the plain GEMV on the K-sliced kernel, which the fused one extends (the default at
+    # M <= 8, the whole-K strip kernel, sums in another order)
     old = tl.set_option(tl.OPT_GEMV_SPLIT, 0)
+    old_impl = tl.set_option(tl.OPT_BITCOS_GEMV, 1)
     yield lambda sk: tl.set_option(tl.OPT_GEMV_SPLIT, sk)
     tl.set_option(tl.OPT_GEMV_SPLIT, old)
+    tl.set_option(tl.OPT_BITCOS_GEMV, old_impl)
 
 
 @pytest.mark.parametrize("bf16", [0, 1])

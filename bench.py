@@ -735,7 +735,8 @@ def int8_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
 # ----------------------------------------------------------------------------- C4: BITCOS + Hadamard
 # K=5376, N=21504, zero fraction z in {0.2, 0.35, 0.5}, M in {1, 8, 512}, fp16; the
 # activations go through the sign flip + FWHT (HB=256: the config's 1024 does not divide 5376)
-# and then the BITCOS GEMV (M <= 8) or the M-tiled GEMM (M = 512).  Bytes as the reference's
+# and then the BITCOS GEMV (M <= 8; at M <= 4 in one launch, ternocl_bitcos_upcvt_hadamard,
+# both timings recorded) or the M-tiled GEMM (M = 512: hadamard_fwht, then the GEMM).  Bytes as the reference's
 # model (bitcos_fp16_upcvt/main.cpp:286-300): the BITCOS buffer + scales (+ A and C).
 BITCOS = dict(K=5376, N=21504, z=(0.2, 0.35, 0.5), M=(1, 8, 512), HB=256, sets=3)
 BITCOS_METRIC = "M=1 BITCOS GEMV weight-stream HBM GB/s (Hadamard pre-transform included, K=5376 N=21504)"
@@ -775,15 +776,30 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
                                                                  S[z].data_ptr(), srs[z][i].data_ptr(), LS,
                                                                  C[M].data_ptr(), None, None, M, N, K, 0, 0, 0, 0, sp))
 
+    def fused(M, z, i):
+        # the transform and the GEMV in one launch (the strip kernel at M <= 8)
+        check(tl, "ternocl_bitcos_upcvt_hadamard",
+              L.ternocl_bitcos_upcvt_hadamard(A[M].data_ptr(), signs.data_ptr(), 1, HB, bufs[z][i].data_ptr(),
+                                              S[z].data_ptr(), srs[z][i].data_ptr(), LS, C[M].data_ptr(), None, None,
+                                              M, N, K, 0, 0, 0, sp))
+
     per = []
     for M in BITCOS["M"]:
         for z in BITCOS["z"]:
             ctr = [0]
 
-            def pipeline(M=M, z=z):
+            def two_kernels(M=M, z=z):
                 had(M)
                 gemv(M, z, ctr[0] % BITCOS["sets"])
                 ctr[0] += 1
+
+            def one_launch(M=M, z=z):
+                fused(M, z, ctr[0] % BITCOS["sets"])
+                ctr[0] += 1
+
+            # one launch where it measured faster (M = 1: 32.9 against 36.7 us); at M = 8 each
+            # CTA's transform of 8 rows costs more than the standalone kernel (41.0 against 39.8)
+            pipeline = one_launch if M <= 4 else two_kernels
 
             def alone(M=M, z=z):
                 gemv(M, z, ctr[0] % BITCOS["sets"])
@@ -793,9 +809,15 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
             for _ in range(warmup):
                 pipeline()
             t_pipe = time_events(stream, pipeline, reps)
+            t_two = time_events(stream, two_kernels, reps) if pipeline is one_launch else t_pipe
+            t_one = time_events(stream, one_launch, reps) if M <= 8 and pipeline is not one_launch else t_pipe
             t_gemv = time_events(stream, alone, reps)
             wbytes = host_bufs[z][0].size * 4 + (K // 128) * N * 2
-            per.append(dict(M=M, z=z, us_per_call=t_pipe * 1e3, gemv_us=t_gemv * 1e3, weight_bytes=wbytes,
+            per.append(dict(M=M, z=z, us_per_call=t_pipe * 1e3, two_kernel_us=t_two * 1e3,
+                            one_launch_us=t_one * 1e3 if M <= 8 else None, gemv_us=t_gemv * 1e3,
+                            launch="fused transform + GEMV" if M <= 4 else
+                            "hadamard_fwht, then GEMV" if M <= 8 else "hadamard_fwht, then GEMM",
+                            weight_bytes=wbytes,
                             GBps=wbytes / (t_pipe * 1e-3) / 1e9 if M <= 8 else None,
                             TFLOPs=2.0 * M * N * K / (t_pipe * 1e-3) / 1e12))
     m1 = [q for q in per if q["M"] == 1]
@@ -812,7 +834,7 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
                       "per_call": per},
            "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                         "peak_kind": peak_kind, "kernel": "bitcos GEMV, M=1, z=0.35 (alone)", "traffic": None},
-           "gpu_launches": 2 * steps * len(m1), "cpu_baseline": None, "e2e": None}
+           "gpu_launches": steps * len(m1), "cpu_baseline": None, "e2e": None}
     if e2e:
         hA = A[1].cpu().pin_memory()
         hC = torch.empty(1, N, dtype=torch.float16).pin_memory()
@@ -820,8 +842,7 @@ def bitcos_measure(tl, dev, steps, warmup, cpu=True, e2e=True):
         for it in range(steps):
             for z in BITCOS["z"]:
                 A[1].copy_(hA, non_blocking=True)
-                had(1)
-                gemv(1, z, it % BITCOS["sets"])
+                fused(1, z, it % BITCOS["sets"])
                 hC.copy_(C[1], non_blocking=True)
                 stream.synchronize()
                 tot += host_bufs[z][0].size * 4 + (K // 128) * N * 2

@@ -264,9 +264,12 @@ int ternocl_hadamard_fwht(const void *x, const int8_t *signs, void *y, int rows,
 /* Hadamard-transformed BITCOS GEMV: ternocl_hadamard_fwht of A (signs, use_signs, hb)
  * followed by ternocl_bitcos_upcvt on the result, in one launch with the transform done
  * while the GEMV stages its activation slice (no intermediate in global memory).  The
- * transformed activations are bit-identical to ternocl_hadamard_fwht's; the GEMV splits
- * K on hb boundaries.  hb in {256, 512, 1024}, K % hb == 0, signs 16-byte aligned.
- * Runs the GEMV kernel for every M (8-row blocks). */
+ * transformed activations are bit-identical to ternocl_hadamard_fwht's.  At M <= 8 (and
+ * TERNOCL_OPT_BITCOS_GEMV 0) the persistent strip kernel runs it, each CTA transforming
+ * its rows once while its first strips load: the output equals the two-kernel pipeline's
+ * bit for bit.  Otherwise the K-sliced GEMV kernel (8-row blocks) splits K on hb
+ * boundaries and transforms each slice.  hb in {256, 512, 1024}, K % hb == 0, signs
+ * 16-byte aligned. */
 int ternocl_bitcos_upcvt_hadamard(const void *A, const int8_t *signs, int use_signs, int hb, const uint32_t *B,
                                   const void *S, const uint32_t *SR, int ls, void *C, const void *Other,
                                   const void *Bias, int M, int N, int K, int dtype, int postop, int out_f32,

@@ -515,6 +515,9 @@ int ternocl_bitcos_upcvt_hadamard(const void *A, const int8_t *signs, int use_si
     a.had_hb = hb;
     a.had_signs = use_signs ? signs : nullptr;
     a.stream = (cudaStream_t)stream;
+    // M <= 8: the strip kernel, each CTA transforming its staged rows once
+    if (options().bitcos_gemv == 0 && bitcos_gemv_p_smem(M, K) > 0)
+        return cuda_status(bitcos_gemv_p_launch(a, sm_count()));
     const GemvPlan p = gemv_bitcos_plan(M, N, K, false, hb);
     if (bitcos_gemv_smem(M, K, p.SK, hb) > 227 * 1024) return TERNOCL_ERR_WORKSPACE;
     a.SK = p.SK;

@@ -66,72 +66,6 @@ __host__ __device__ inline size_t bitcos_smem_bytes(int rows, int ng, bool had =
            (size_t)32 * sign_cap(ng) * 4 + (size_t)rows * ((size_t)ng * kGS * 2 + 16) + (had ? (size_t)ng * kGS : 0);
 }
 
-// Sign flip + FWHT, in place, of HB = 32 E-wide blocks of the CTA's staged activation rows
-// [rows x krange] (the swizzled units of step 5; sgn = the range's signs, staged or null):
-// one warp per block, lane l holding elements E l .. E l + E - 1, the stages of stride
-// 1 .. E/2 in registers and those of stride E .. HB/2 across lanes (__shfl_xor), every
-// stage the fp32 pair (a + b, a - b), in increasing stride order as hadamard_fwht, then
-// the scale and the DT rounding of the standalone kernel.
-template <class DT, int E>
-__device__ void stage_fwht(const gemv::Params &p, char *act, int act_stride, const int8_t *sgn, int rows,
-                           int krange, int warp, int lane) {
-    constexpr int HB = 32 * E;
-    const int nb = krange / HB, total = rows * nb;
-    for (int blk = warp; blk < total; blk += gemv::kWarps) {
-        const int m = blk / nb, k0 = (blk % nb) * HB + lane * E;  // within the range
-        char *row = act + (size_t)m * act_stride;
-        float v[E];
-#pragma unroll
-        for (int q = 0; q < E / 8; ++q) {
-            const int u = k0 / 8 + q;
-            const uint4 w4 = *reinterpret_cast<const uint4 *>(row + (size_t)(u ^ (((u >> 3) & 1) << 1)) * 16);
-            const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                v[8 * q + 2 * j] = DT::tof((uint16_t)(w[j] & 0xffffu));
-                v[8 * q + 2 * j + 1] = DT::tof((uint16_t)(w[j] >> 16));
-            }
-        }
-        if (sgn) {
-#pragma unroll
-            for (int q = 0; q < E / 8; ++q) {  // 8 signs per 8-byte read
-                const uint2 sv = *reinterpret_cast<const uint2 *>(sgn + k0 + 8 * q);
-                const uint32_t sw[2] = {sv.x, sv.y};
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[8 * q + j] *= (float)(int8_t)((sw[j >> 2] >> (8 * (j & 3))) & 0xffu);
-            }
-        }
-#pragma unroll
-        for (int h = 1; h < E; h <<= 1)
-#pragma unroll
-            for (int j = 0; j < E; ++j)
-                if ((j & h) == 0) {
-                    const float a = v[j], b = v[j + h];
-                    v[j] = a + b;
-                    v[j + h] = a - b;
-                }
-#pragma unroll
-        for (int c = 0; c < 5; ++c) {  // stride E << c: lane bit c
-            const bool upper = (lane >> c) & 1;
-#pragma unroll
-            for (int j = 0; j < E; ++j) {
-                const float o = __shfl_xor_sync(0xffffffffu, v[j], 1 << c);
-                v[j] = upper ? o - v[j] : v[j] + o;
-            }
-        }
-#pragma unroll
-        for (int q = 0; q < E / 8; ++q) {
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                w[j] = (uint32_t)DT::fromf(v[8 * q + 2 * j] * p.had_scale) |
-                       ((uint32_t)DT::fromf(v[8 * q + 2 * j + 1] * p.had_scale) << 16);
-            const int u = k0 / 8 + q;
-            *reinterpret_cast<uint4 *>(row + (size_t)(u ^ (((u >> 3) & 1) << 1)) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-    }
-}
-
 template <class DT, int POSTOP, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Params p) {
     extern __shared__ __align__(128) char smem[];
@@ -263,9 +197,9 @@ __global__ void __launch_bounds__(kThreads) bitcos_gemv_kernel(const gemv::Param
     __syncthreads();
     if (p.had_L) {
         const int8_t *sg = p.had_signs ? sgn : nullptr;
-        if (p.had_L == 8) stage_fwht<DT, 8>(p, act, act_stride, sg, rows, krange, warp, lane);
-        else if (p.had_L == 9) stage_fwht<DT, 16>(p, act, act_stride, sg, rows, krange, warp, lane);
-        else stage_fwht<DT, 32>(p, act, act_stride, sg, rows, krange, warp, lane);
+        if (p.had_L == 8) fwht::staged_rows<DT, 8>(act, act_stride, sg, rows, krange, p.had_scale, warp, gemv::kWarps, lane);
+        else if (p.had_L == 9) fwht::staged_rows<DT, 16>(act, act_stride, sg, rows, krange, p.had_scale, warp, gemv::kWarps, lane);
+        else fwht::staged_rows<DT, 32>(act, act_stride, sg, rows, krange, p.had_scale, warp, gemv::kWarps, lane);
         __syncthreads();
     }
 

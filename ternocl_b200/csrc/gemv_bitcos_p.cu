@@ -21,7 +21,10 @@
 //     window) as one 1-D bulk copy widened to 16-byte boundaries; the word offset inside
 //     the slot is written beside the stage.
 // The activation rows are staged once per CTA (after griddepcontrol.wait), with the
-// 16-byte units swizzled as in the other GEMVs.
+// 16-byte units swizzled as in the other GEMVs; with the fused Hadamard transform (the
+// reference's hadamard_fwht -> BITCOS GEMV pipeline) the compute warps sign-flip and
+// transform them in place, the stages of hadamard_fwht in its order (bit-identical to
+// the standalone kernel), while the first strips load.
 //
 // nw compute warps (8-16, chosen so they split the K/128 groups evenly) take
 // contiguous group ranges of the strip.  Per strip: each warp popcounts its bitmap rows
@@ -41,11 +44,13 @@
 // epilogue.  Every mbarrier wait is bounded (tc::mbar_wait); a timeout flags the device
 // error word, and the compute warps leave together through a shared abort flag checked
 // after a named barrier.
+#include <cmath>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
 #include "gemv_common.cuh"
+#include "hadamard_common.cuh"
 #include "launch.h"
 #include "tc_common.cuh"
 
@@ -68,6 +73,11 @@ struct Params {
     int KW, G, cap;          // bitmap rows, scale groups, sign words per column slot
     int act_stride;          // bytes per staged activation row
     int box_b, box_s;        // rows per TMA box of the bitmap / scale plane (divide KW / G)
+    // the reference's hadamard_fwht -> BITCOS GEMV pipeline in one launch: log2 of the
+    // FWHT block (0: none), its sign vector [K] (global, or null) and 1/sqrt(HB)
+    int had_L;
+    const int8_t *had_signs;
+    float had_scale;
     // shared-memory layout (byte offsets)
     int o_red, o_seg, o_meta, o_bars, o_act, o_stage, stage_bytes, o_sc, o_sg, total;
 };
@@ -264,6 +274,11 @@ __global__ void __launch_bounds__((kMaxNW + 1) * 32, 1)
 
     // compute warps: warp w owns groups wg0 .. wg1 - 1 of every strip; lane (g, q)
     const int w = warp, g = lane >> 2, q = lane & 3;
+    // the fused transform: every CTA turns its staged rows once, while the first strips
+    // are still in flight (visible to all compute warps after the first named barrier)
+    if (p.had_L == 8) fwht::staged_rows<DT, 8>(act, p.act_stride, p.had_signs, rows, K, p.had_scale, w, nw, lane);
+    else if (p.had_L == 9) fwht::staged_rows<DT, 16>(act, p.act_stride, p.had_signs, rows, K, p.had_scale, w, nw, lane);
+    else if (p.had_L == 10) fwht::staged_rows<DT, 32>(act, p.act_stride, p.had_signs, rows, K, p.had_scale, w, nw, lane);
     const int wg0 = G * w / nw, wg1 = G * (w + 1) / nw;
     const uint2 *lut_lane = lut + (lane & ((1 << LUT_SH) - 1));
     uint32_t *seg = reinterpret_cast<uint32_t *>(smem + p.o_seg);  // [nw][32]
@@ -466,6 +481,9 @@ cudaError_t bitcos_gemv_p_launch(const GemvArgs &a, int sms) {
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
+    p.had_L = a.had_hb ? 31 - __builtin_clz((unsigned)a.had_hb) : 0;
+    p.had_signs = a.had_signs;
+    p.had_scale = a.had_hb ? (float)(1.0 / std::sqrt((double)a.had_hb)) : 1.0f;
     p.box_b = box_rows(p.KW);
     p.box_s = box_rows(p.G);
     CUtensorMap tmB, tmS;

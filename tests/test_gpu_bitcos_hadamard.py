@@ -50,6 +50,22 @@ def test_matches_two_kernels(cuda, tl, split, M, K, N, hb, sk, bf16):
 
 
 @pytest.mark.parametrize("bf16", [0, 1])
+@pytest.mark.parametrize("M,K,N,hb", [(1, 5376, 512, 256), (8, 5376, 272, 256), (3, 4096, 256, 1024),
+                                      (1, 4096, 1024, 512), (2, 1024, 48, 256)])
+def test_strip_kernel_matches_two_kernels(cuda, tl, M, K, N, hb, bf16):
+    # M <= 8 on the whole-K strip kernel: each CTA transforms its staged rows once, with
+    # the standalone kernel's stages, so the result is the two-kernel pipeline's bit for bit
+    assert tl.set_option(tl.OPT_BITCOS_GEMV, 0) in (0, 1)
+    A, buf, S, s = case(tl, 7 * M + K + hb, M, K, N, 0.35, bf16)
+    dA, dB, dS, ds = dev_dt(A, bf16), dev_words(buf), dev_dt(S, bf16), dev_any(s)
+    for signs in (ds, None):
+        fused = host_dt(tl.bitcos_upcvt_hadamard(dA, dB, dS, hb, signs=signs))
+        two = host_dt(tl.bitcos_upcvt(tl.hadamard_fwht(dA, hb, signs=signs), dB, dS))
+        assert np.array_equal(fused, two), (M, K, N, hb, signs is not None)
+    assert tl.device_error() == 0
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
 @pytest.mark.parametrize("M,K,N,ls", [(1, 5376, 512, 1), (8, 5376, 512, 4), (2, 5376, 2048, 7), (4, 1024, 96, 2)])
 def test_vs_oracle(cuda, tl, M, K, N, ls, bf16):
     # C4 shape: K = 5376 transforms with HB = 256 (5376 % 1024 != 0)

@@ -202,8 +202,40 @@ inline bool compare_f32(const float *C, const float *G, size_t n, const std::str
     return bad == 0;
 }
 
+// The relative error this library is held to beside the reference's pass rule (which
+// at these input scales admits almost any output through its absolute bound):
+// max |C - G| / max(|G|, f * rms(G)), f = 1e-2 for DT outputs (tolerance 2e-3 fp16,
+// 1e-2 bf16) and 0.25 for fp32 outputs (2e-4), as tests/helpers.py checks it.  Printed
+// only; the pass/fail status stays the reference's.
+inline void report_rel(const Epilogue &e, const unsigned char *C, const unsigned char *G, size_t n,
+                       const std::string &label) {
+    auto val = [&](const unsigned char *X, size_t i) -> double {
+        if (e.out_f32) {
+            float v;
+            std::memcpy(&v, X + 4 * i, 4);
+            return v;
+        }
+        uint16_t h;
+        std::memcpy(&h, X + 2 * i, 2);
+        return tof(h);
+    };
+    double ss = 0.0;
+    for (size_t i = 0; i < n; ++i) ss += val(G, i) * val(G, i);
+    const double floor = (e.out_f32 ? 0.25 : 1e-2) * std::sqrt(ss / (double)(n ? n : 1));
+    double r = 0.0;
+    for (size_t i = 0; i < n; ++i) {
+        const double g = val(G, i), d = std::fabs(val(C, i) - g);
+        const double q = d / std::max(std::max(std::fabs(g), floor), 1e-30);
+        r = std::max(r, std::isnan(q) ? INFINITY : q);
+    }
+    const double tol = e.out_f32 ? 2e-4 : (bf16_mode() ? 1e-2 : 2e-3);
+    std::cout << label << ": max rel err " << r << " (tolerance " << tol << ": " << (r <= tol ? "within" : "OVER")
+              << ")\n";
+}
+
 inline bool compare_out(const Epilogue &e, const unsigned char *C, const unsigned char *G, size_t n,
                         const std::string &label) {
+    report_rel(e, C, G, n, label);
     if (e.out_f32) return compare_f32((const float *)C, (const float *)G, n, label);
     return compare_dt((const uint16_t *)C, (const uint16_t *)G, n, label, e.abs_tol(), e.ulp_tol());
 }

@@ -16,6 +16,7 @@ DRIVERS = ["int2_fp16_upcvt", "int1_fp16_upcvt", "int2_int8", "bitcos_fp16_upcvt
 
 AVG_DEV = re.compile(r"^Avg dev   time: [0-9.]+ ms \([0-9.]+ GFLOPS, [0-9.]+ GiB/s", re.M)
 VALID = re.compile(r"^Validation summary: (\d+)/(\d+) sets PASSED$", re.M)
+REL = re.compile(r"^validation \[set 0/\d+\]: max rel err \S+ \(tolerance \S+: within\)$", re.M)
 COMPARE = re.compile(r"^validation \[set 0/\d+\]: max abs diff \S+ (\(idx \d+\), max ULP diff \d+ \(idx \d+\)|, max rel diff \S+), "
                      r"pass rate 100%$", re.M)
 
@@ -53,6 +54,8 @@ def test_validates(name, dtype, m):
     out = r.stdout
     assert AVG_DEV.search(out), out
     assert COMPARE.search(out), out
+    # beside the reference's rule: the relative error the tests hold the library to
+    assert REL.search(out), out
     assert VALID.search(out).groups() == ("2", "2"), out
     if name == "int2_int8":
         assert re.search(r"^scale_a: 0/\d+ differ from host$", out, re.M), out

@@ -89,6 +89,11 @@ def test_options():
     assert L.ternocl_set_option(2, 100) == -1  # GEMM tile rows: 0, 128 or 256
     assert L.ternocl_set_option(2, 256) == 0 and L.ternocl_set_option(2, 0) == 256
     assert L.ternocl_set_option(99, 1) == -1
+    # the BITCOS GEMV choice (9): 0 strip kernel at M <= 8, 1 the K-sliced kernel
+    assert L.ternocl_set_option(9, 2) == -1
+    assert L.ternocl_set_option(9, 1) == 0 and L.ternocl_set_option(9, 0) == 1
+    # removed values and the reserved option answer -1 (6: GEMV_IMPL 0..2, 7: reserved)
+    assert L.ternocl_set_option(6, 3) == -1 and L.ternocl_set_option(7, 4) == -1
 
 
 def test_host_bitcos_packer_roundtrip():

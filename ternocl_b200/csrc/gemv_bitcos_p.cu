@@ -26,10 +26,10 @@
 // transform them in place, the stages of hadamard_fwht in its order (bit-identical to
 // the standalone kernel), while the first strips load.
 //
-// nw compute warps (8-16, chosen so they split the K/128 groups evenly) take
-// contiguous group ranges of the strip.  Per strip: each warp popcounts its bitmap rows
-// (lane = column), a named barrier, and the warp's start rank per column is the sum of
-// the earlier warps' counts.  The main loop per group is the nibble decode of the
+// nw compute warps (one per group up to 16, else 16) take contiguous group ranges of the
+// strip, sized so that the SM's four schedulers get equal shares.  Per strip: each warp
+// popcounts its bitmap rows (lane = column), a named barrier, and the warp's start rank
+// per column is the sum of the earlier warps' counts.  The main loop per group is the nibble decode of the
 // K-sliced kernel (gemv_bitcos.cu): lane (g, q) takes bitmap word q of columns
 // 4g..4g+3, a 4-lane scan gives each word's rank, a 32-bit sign window comes out of the
 // staged stream with one funnel shift, and each 4-row nibble indexes the 256-entry
@@ -73,6 +73,7 @@ struct Params {
     int KW, G, cap;          // bitmap rows, scale groups, sign words per column slot
     int act_stride;          // bytes per staged activation row
     int box_b, box_s;        // rows per TMA box of the bitmap / scale plane (divide KW / G)
+    int wg[kMaxNW + 1];      // compute warp w owns groups wg[w] .. wg[w+1] - 1 of a strip
     // the reference's hadamard_fwht -> BITCOS GEMV pipeline in one launch: log2 of the
     // FWHT block (0: none), its sign vector [K] (global, or null) and 1/sqrt(HB)
     int had_L;
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__((kMaxNW + 1) * 32, 1)
     extern __shared__ __align__(128) char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nw = p.nw, nthreads = (nw + 1) * 32;
-    const int N = p.N, K = p.K, G = p.G;
+    const int N = p.N, K = p.K;
     const int nstrips = (N + 31) / 32;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.o_bars);
     uint64_t *empty = full + kMaxStages;
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__((kMaxNW + 1) * 32, 1)
     if (p.had_L == 8) fwht::staged_rows<DT, 8>(act, p.act_stride, p.had_signs, rows, K, p.had_scale, w, nw, lane);
     else if (p.had_L == 9) fwht::staged_rows<DT, 16>(act, p.act_stride, p.had_signs, rows, K, p.had_scale, w, nw, lane);
     else if (p.had_L == 10) fwht::staged_rows<DT, 32>(act, p.act_stride, p.had_signs, rows, K, p.had_scale, w, nw, lane);
-    const int wg0 = G * w / nw, wg1 = G * (w + 1) / nw;
+    const int wg0 = p.wg[w], wg1 = p.wg[w + 1];
     const uint2 *lut_lane = lut + (lane & ((1 << LUT_SH) - 1));
     uint32_t *seg = reinterpret_cast<uint32_t *>(smem + p.o_seg);  // [nw][32]
     float *red = reinterpret_cast<float *>(smem + p.o_red);         // [nw][8][32]
@@ -425,21 +426,25 @@ static int box_rows(int x) {
     return 1;
 }
 
-// Compute warps for G groups: 8..16 warps with the fewest idle group slots
-// (G / (nw * ceil(G / nw)) largest; the larger nw on a tie); G itself when G <= 16.
-static int pick_nw(int G) {
-    if (G <= kMaxNW) return G;
-    int best = 8;
-    double be = 0.0;
-    for (int nw = 8; nw <= kMaxNW; ++nw) {
-        const int per = (G + nw - 1) / nw;
-        const double eff = (double)G / ((double)nw * per);
-        if (eff >= be) {
-            be = eff;
-            best = nw;
-        }
+// Compute warps for G groups: one per group up to 16, else 16 (four per scheduler).
+static int pick_nw(int G) { return G < kMaxNW ? G : kMaxNW; }
+
+// Contiguous group ranges of the nw compute warps, sized so that each of the SM's four
+// schedulers (warp w issues on scheduler w % 4) gets G/4 groups of a strip (one more for
+// the first G % 4): the warps of one strip meet at named barriers, so the strip takes as
+// long as the busiest scheduler's share.  (14 warps of 3 groups at G = 42 gave schedulers
+// 12, 12, 9 and 9 groups; 16 warps split this way give 11, 11, 10, 10.)
+static void split_groups(int G, int nw, int wg[kMaxNW + 1]) {
+    int size[kMaxNW] = {};
+    for (int sch = 0; sch < 4; ++sch) {
+        const int total = G / 4 + (sch < G % 4 ? 1 : 0);
+        int cnt = 0;
+        for (int w = sch; w < nw; w += 4) ++cnt;
+        int j = 0;
+        for (int w = sch; w < nw; w += 4, ++j) size[w] = total / cnt + (j < total % cnt ? 1 : 0);
     }
-    return best;
+    wg[0] = 0;
+    for (int w = 0; w < nw; ++w) wg[w + 1] = wg[w] + size[w];
 }
 
 }  // namespace bitcos_p
@@ -484,6 +489,7 @@ cudaError_t bitcos_gemv_p_launch(const GemvArgs &a, int sms) {
     p.had_L = a.had_hb ? 31 - __builtin_clz((unsigned)a.had_hb) : 0;
     p.had_signs = a.had_signs;
     p.had_scale = a.had_hb ? (float)(1.0 / std::sqrt((double)a.had_hb)) : 1.0f;
+    split_groups(p.G, p.nw, p.wg);
     p.box_b = box_rows(p.KW);
     p.box_s = box_rows(p.G);
     CUtensorMap tmB, tmS;

@@ -202,20 +202,18 @@ __global__ void __launch_bounds__((kMaxNW + 1) * 32, 1)
     }
     __syncthreads();
 
-    // the first stages: weights only, so before the wait on the previous kernel
+    // the first strip: weights only, so before the wait on the previous kernel; the runs of
+    // every first stage are loaded together (one latency), the other first stages are
+    // issued after the CTA-wide barrier below, which they would otherwise hold up (the
+    // copy engine takes ~2 us to accept a strip)
+    Runs r[kMaxStages];
     if (warp == nw) {
-        // the runs of every first stage before any issue: one latency for all of them
-        Runs r[kMaxStages];
 #pragma unroll
         for (int j = 0; j < kMaxStages; ++j) {
             const int s = blockIdx.x + j * gridDim.x;
             r[j] = (j < p.stages && s < nstrips) ? load_runs(p, s, lane) : Runs{0u, 0u};
         }
-#pragma unroll
-        for (int j = 0; j < kMaxStages; ++j) {
-            const int s = blockIdx.x + j * gridDim.x;
-            if (j < p.stages && s < nstrips) issue_strip(p, &tmB, &tmS, smem, full, s, j, lane, r[j]);
-        }
+        if ((int)blockIdx.x < nstrips) issue_strip(p, &tmB, &tmS, smem, full, blockIdx.x, 0, lane, r[0]);
     }
 
     // (presence nibble m, 4 sign bits s) -> DT codes of 4 rows in row order; entry e of
@@ -250,6 +248,11 @@ __global__ void __launch_bounds__((kMaxNW + 1) * 32, 1)
     __syncthreads();
 
     if (warp == nw) {
+#pragma unroll
+        for (int j = 1; j < kMaxStages; ++j) {
+            const int s = blockIdx.x + j * gridDim.x;
+            if (j < p.stages && s < nstrips) issue_strip(p, &tmB, &tmS, smem, full, s, j, lane, r[j]);
+        }
         // producer: the remaining strips, each into the stage its strip - stages freed
         int it = 0, issued = 0;
         const int s_first = blockIdx.x + p.stages * gridDim.x;  // the first strip issued here

@@ -264,8 +264,7 @@ int plan_and_launch_int2_gemv(const void *A, const uint32_t *B, const void *S, v
 int report_cuda(cudaError_t e) { return cuda_status(e); }
 
 size_t int2_gemv_counter_bytes(int M, int N) {
-    // per-strip kernels: one counter per (32-column strip, row block of >= 4 rows);
-    // stream-K: one per strip
+    // one counter per (32-column strip, row block of >= 4 rows)
     const size_t tiles = (size_t)((N + 31) / 32) * (size_t)((M + 3) / 4);
     return round_up(tiles * sizeof(unsigned), 256);
 }

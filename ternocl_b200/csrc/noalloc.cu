@@ -73,8 +73,8 @@ extern "C" int ternocl_int2_upcvt_noalloc(const void *A, const uint32_t *B, cons
     if (M == 0) return TERNOCL_OK;
 
     // The GEMV runs exactly as ternocl_int2_upcvt plans it for a workspace of the
-    // array's size: the stream-K kernel or the per-strip kernels, with the split the
-    // plan picks (none where it picks none).  A plan whose scratch would not fit the
+    // array's size: the same per-strip kernel, warps and split the plan picks (none
+    // where it picks none).  A plan whose scratch would not fit the
     // array falls back to the forms that need none; a shape no form can run is refused.
     void *scratch = nullptr;
     cudaError_t e = scratch_ptr(&scratch);

@@ -23,7 +23,7 @@ pytestmark = pytest.mark.gpu
 SCRATCH = 16 << 20
 
 CASES = [
-    (1, 4096, 4096, 0, 0),    # stream-K integer-MMA GEMV, split strips summed in the array
+    (1, 4096, 4096, 0, 0),    # integer-MMA GEMV, one CTA per 32-column strip (no split)
     (3, 2048, 1024, 1, 0),    # the same at M = 3
     (8, 1024, 512, 0, 3),     # fp16-MMA GEMV (M > 4) with a K split
     (1, 14336, 512, 1, 1),

@@ -107,6 +107,9 @@ int ternocl_device_error(int reset);
  *    0 = at M <= 8 the persistent kernel (one CTA per SM over whole-K strips of 32
  *    columns; LS and SR are not read), else the K-sliced kernel; 1 = always the K-sliced
  *    kernel (the reference's LS split with slice ranks).
+ * Options are process-wide and every call reads them when it plans its launch; setting
+ * one from any thread while others call the library is safe (each is an atomic value, so
+ * a call sees the old or the new setting).
  * Returns the previous value, or -1 for an unknown option or value. */
 typedef enum {
     TERNOCL_OPT_PDL = 1,

@@ -73,7 +73,7 @@ static GemvPlan gemv_plan_t(int M, int N, int K, int cols, int rows, int per_sm,
     const long long tiles = (long long)strips * zb;
     const long long target = (long long)per_sm * sm_count();
     int sk = (int)((target + tiles - 1) / tiles);
-    if (options().gemv_split) sk = options().gemv_split;
+    if (const int forced = options().gemv_split) sk = forced;
     if (sk > G) sk = G;
     if (sk > 64) sk = 64;
     while (sk < G && smem_of_sk(sk) > smem_budget) ++sk;
@@ -102,7 +102,8 @@ static GemvPlan gemv_plan(int M, int N, int K, bool allow_ws) {
     const int G = K / kGS, sms = sm_count();
     const long long tiles = (long long)((N + 31) / 32) * ((M + 7) / 8);
     const bool wide = M > kGemvDigitMaxM;
-    int sk = options().gemv_split ? options().gemv_split : (wide ? 2 : (tiles < sms ? 2 : 1));
+    const int forced = options().gemv_split;
+    int sk = forced ? forced : (wide ? 2 : (tiles < sms ? 2 : 1));
     if (sk > G) sk = G;
     int warps = options().gemv_warps;
     if (!warps) {
@@ -140,9 +141,10 @@ static GemvPlan gemv_digit_plan(int M, int N, int K, bool allow_ws) {
     const int dwarps = tiles >= 4LL * sms ? 4 : 8;
     if (2 * tiles < sms) sk = 2;
     else if (tiles >= sms && tiles < 2LL * sms && G >= 64) sk = 2;
-    if (options().gemv_split) sk = options().gemv_split;
+    if (const int forced = options().gemv_split) sk = forced;
     if (sk > G) sk = G;
-    const int warps = options().gemv_warps ? options().gemv_warps : dwarps;
+    const int forced_warps = options().gemv_warps;
+    const int warps = forced_warps ? forced_warps : dwarps;
     GemvPlan p;
     p.SK = sk;
     while (p.SK < G && int2_gemv_d_smem(M, K, p.SK, warps) > kGemvSmemBudget) ++p.SK;
@@ -327,51 +329,35 @@ const char *ternocl_last_error(void) { return g_last_error; }
 
 int ternocl_set_option(int option, int value) {
     if (option == TERNOCL_OPT_PDL) {
-        const int old = options().pdl;
-        options().pdl = value ? 1 : 0;
-        return old;
+        return options().pdl.exchange(value ? 1 : 0);
     }
     if (option == TERNOCL_OPT_GEMM_PERSISTENT) {
         if (value < 0 || value > 3) return -1;
-        const int old = options().gemm_persistent;
-        options().gemm_persistent = value;
-        return old;
+        return options().gemm_persistent.exchange(value);
     }
     if (option == TERNOCL_OPT_GEMV_WARPS) {
         if (value != 0 && value != 4 && value != 8 && value != 16) return -1;
-        const int old = options().gemv_warps;
-        options().gemv_warps = value;
-        return old;
+        return options().gemv_warps.exchange(value);
     }
     if (option == TERNOCL_OPT_GEMV_SPLIT) {
         if (value < 0 || value > 64) return -1;
-        const int old = options().gemv_split;
-        options().gemv_split = value;
-        return old;
+        return options().gemv_split.exchange(value);
     }
     if (option == TERNOCL_OPT_GEMV_IMPL) {
         if (value < 0 || value > 2) return -1;
-        const int old = options().gemv_impl;
-        options().gemv_impl = value;
-        return old;
+        return options().gemv_impl.exchange(value);
     }
     if (option == TERNOCL_OPT_BITCOS_GEMV) {
         if (value < 0 || value > 1) return -1;
-        const int old = options().bitcos_gemv;
-        options().bitcos_gemv = value;
-        return old;
+        return options().bitcos_gemv.exchange(value);
     }
     if (option == TERNOCL_OPT_PEER_TIMEOUT_MS) {
         if (value < 1 || value > 60000) return -1;
-        const int old = options().peer_timeout_ms;
-        options().peer_timeout_ms = value;
-        return old;
+        return options().peer_timeout_ms.exchange(value);
     }
     if (option == TERNOCL_OPT_GEMM_TILE_M) {
         if (value != 0 && value != 128 && value != 256) return -1;
-        const int old = options().gemm_tile_m;
-        options().gemm_tile_m = value;
-        return old;
+        return options().gemm_tile_m.exchange(value);
     }
     return -1;
 }

@@ -657,7 +657,7 @@ namespace gemm {
 // 256-row tile does twice the work of a 128-row one in ~1.6x the time (measured on
 // B200), so pick the shape with fewer wave-weighted units.
 bool use_256_rows(int M, int N) {
-    if (options().gemm_tile_m) return options().gemm_tile_m == 256;
+    if (const int tile_m = options().gemm_tile_m) return tile_m == 256;
     if (M <= BM) return false;
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -687,7 +687,8 @@ cudaError_t moe_gemm_tc_launch(const GemvArgs &a, const int *meta, int E) {
     const int pers = options().gemm_persistent;
     if (pers == 1 || pers == 2 || (pers == 3 && a.K <= 1024))
         return gemm::launch_persistent<gemm::Int2Gemm>(a, meta, E);
-    const bool rows256 = options().gemm_tile_m ? options().gemm_tile_m == 256 : a.M >= 2 * gemm::BM * E;
+    const int tile_m = options().gemm_tile_m;
+    const bool rows256 = tile_m ? tile_m == 256 : a.M >= 2 * gemm::BM * E;
     return rows256 ? gemm::launch_policy<gemm::Int2Gemm, 2>(a, meta, E)
                    : gemm::launch_policy<gemm::Int2Gemm, 1>(a, meta, E);
 }

@@ -4,6 +4,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <type_traits>
 
 #include "ternocl.h"
@@ -13,17 +14,21 @@ namespace ternocl {
 struct F16;
 struct BF16;
 
-// Process-wide options (ternocl_set_option).
+// Process-wide options (ternocl_set_option), read by every call: atomic, so that a
+// thread setting one while others launch is no data race (a call sees the old or the
+// new value, never a torn one).
 struct Options {
-    int pdl = 0;          // launch with programmatic stream serialization
-    int gemm_tile_m = 0;  // prefill GEMM CTA rows: 0 = per shape, 128 or 256
-    int gemv_split = 0;   // decode GEMV K split: 0 = planned per shape
-    int gemv_warps = 0;   // decode GEMV warps per CTA: 0 = planned per shape
-    int gemm_persistent = 3;  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every prefill GEMM,
-                              // 3 MoE grouped GEMMs with K <= 1024
-    int gemv_impl = 0;        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA per strip (M <= 4)
-    int peer_timeout_ms = 2000;  // limit of the column-sharded GEMV's wait for its peers
-    int bitcos_gemv = 0;         // BITCOS decode GEMV: 0 persistent strip kernel where it applies, 1 K-sliced
+    std::atomic<int> pdl{0};          // launch with programmatic stream serialization
+    std::atomic<int> gemm_tile_m{0};  // prefill GEMM CTA rows: 0 = per shape, 128 or 256
+    std::atomic<int> gemv_split{0};   // decode GEMV K split: 0 = planned per shape
+    std::atomic<int> gemv_warps{0};   // decode GEMV warps per CTA: 0 = planned per shape
+    std::atomic<int> gemm_persistent{3};  // persistent tcgen05 GEMM: 0 never, 1 MoE grouped GEMMs, 2 every
+                                          // prefill GEMM, 3 MoE grouped GEMMs with K <= 1024
+    std::atomic<int> gemv_impl{0};        // int2 decode GEMV: 0 per M, 1 fp16 MMA decode, 2 integer MMA per
+                                          // strip (M <= 4)
+    std::atomic<int> peer_timeout_ms{2000};  // limit of the column-sharded GEMV's wait for its peers
+    std::atomic<int> bitcos_gemv{0};         // BITCOS decode GEMV: 0 persistent strip kernel where it applies,
+                                             // 1 K-sliced
 };
 Options &options();
 
